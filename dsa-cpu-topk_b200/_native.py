@@ -1,0 +1,132 @@
+"""ctypes binding of libdsa_b200.so (the C ABI in include/dsa_b200.h).
+
+The library is loaded from this directory.  There is no fallback: if it is
+missing or a call fails, an exception is raised.  Tensors passed in must be
+CUDA tensors on the current device, contiguous and 16-byte aligned; the
+wrappers in lightning_indexer.py / dsa_attention.py make sure of that.
+Every call is enqueued on torch's current CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdsa_b200.so")
+
+DSA_OK, DSA_ERR_INVALID, DSA_ERR_UNSUPPORTED, DSA_ERR_CUDA = 0, -1, -2, -3
+DSA_F32, DSA_BF16, DSA_F16 = 0, 1, 2
+_DTYPES = {torch.float32: DSA_F32, torch.bfloat16: DSA_BF16, torch.float16: DSA_F16}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loaded on first use)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is not built; run `python dsa-cpu-topk_b200/build.py` "
+                "(or __graft_entry__.build()) first")
+        L = ctypes.CDLL(LIB_PATH)
+        p, i64, i32, f32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+        L.dsa_version.restype = i32
+        L.dsa_last_error_string.restype = ctypes.c_char_p
+        L.dsa_indexer_scores.argtypes = [p, p, p, p, i64, i64, i64, i64, i64, i64, i32, i32, p]
+        L.dsa_topk_select.argtypes = [p, i64, i64, i64, i64, i64, i32, i64, p, p, p, i64, p]
+        L.dsa_sparse_attn_threshold.argtypes = [p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
+                                                f32, i32, p]
+        L.dsa_sparse_attn.argtypes = [p, p, i64, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
+                                      f32, i32, p]
+        L.dsa_forward_workspace_bytes.argtypes = [i64, i64, i64, i64]
+        L.dsa_forward_workspace_bytes.restype = sz
+        L.dsa_forward.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                  i32, i32, p, sz, p]
+        for name in ("dsa_indexer_scores", "dsa_topk_select", "dsa_sparse_attn_threshold",
+                     "dsa_sparse_attn", "dsa_forward"):
+            getattr(L, name).restype = i32
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc == DSA_OK:
+        return
+    msg = f"{what}: {lib().dsa_last_error_string().decode(errors='replace')}"
+    if rc == DSA_ERR_INVALID:
+        raise AssertionError(msg)
+    raise RuntimeError(msg)
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise AssertionError(f"unsupported dtype {t.dtype} (fp32, bf16, fp16)") from None
+
+
+def prep(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous, 16-byte-aligned CUDA tensor (copies only when needed)."""
+    assert t.is_cuda, "inputs must be CUDA tensors"
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def indexer_scores(q, k, w, scores, *, q_row0=0, fill_upper=True):
+    B, T_q, HI, DI = q.shape
+    T_k = k.shape[1]
+    _check(lib().dsa_indexer_scores(_ptr(q), _ptr(k), _ptr(w), _ptr(scores), B, T_q, T_k, q_row0,
+                                    HI, DI, dtype_code(q), int(bool(fill_upper)), _stream()),
+           "dsa_indexer_scores")
+
+
+def topk_select(scores, n_rows, row_len, row_stride, k, thr, idx=None, cnt=None, idx_cap=0, *,
+                causal=False, rows_per_batch=1, q_row0=0):
+    _check(lib().dsa_topk_select(_ptr(scores), n_rows, row_len, row_stride, rows_per_batch, q_row0,
+                                 int(bool(causal)), k, _ptr(thr), _ptr(idx), _ptr(cnt), idx_cap,
+                                 _stream()), "dsa_topk_select")
+
+
+def sparse_attn_threshold(scores, thr, Q, K, V, O, *, q_row0=0, scale=None):
+    B, T_q, HQ, DQ = Q.shape
+    T_k, DV = K.shape[1], V.shape[-1]
+    scale = DQ ** -0.5 if scale is None else scale
+    _check(lib().dsa_sparse_attn_threshold(_ptr(scores), _ptr(thr), _ptr(Q), _ptr(K), _ptr(V),
+                                           _ptr(O), B, T_q, T_k, q_row0, HQ, DQ, DV, scale,
+                                           dtype_code(Q), _stream()), "dsa_sparse_attn_threshold")
+
+
+def sparse_attn(idx, cnt, idx_cap, scores, thr, Q, K, V, O, *, q_row0=0, scale=None):
+    B, T_q, HQ, DQ = Q.shape
+    T_k, DV = K.shape[1], V.shape[-1]
+    scale = DQ ** -0.5 if scale is None else scale
+    _check(lib().dsa_sparse_attn(_ptr(idx), _ptr(cnt), idx_cap, _ptr(scores), _ptr(thr), _ptr(Q),
+                                 _ptr(K), _ptr(V), _ptr(O), B, T_q, T_k, q_row0, HQ, DQ, DV, scale,
+                                 dtype_code(Q), _stream()), "dsa_sparse_attn")
+
+
+def forward_workspace_bytes(B, T_q, T_k, top_k) -> int:
+    return int(lib().dsa_forward_workspace_bytes(B, T_q, T_k, top_k))
+
+
+def forward(q_idx, k_idx, w_idx, Q, K, V, O, top_k, workspace, *, q_row0=0):
+    B, T_q, HI, DI = q_idx.shape
+    T_k = k_idx.shape[1]
+    HQ, DQ, DV = Q.shape[2], Q.shape[3], V.shape[3]
+    _check(lib().dsa_forward(_ptr(q_idx), _ptr(k_idx), _ptr(w_idx), _ptr(Q), _ptr(K), _ptr(V),
+                             _ptr(O), B, T_q, T_k, q_row0, HI, DI, HQ, DQ, DV, top_k,
+                             dtype_code(q_idx), dtype_code(Q), _ptr(workspace),
+                             workspace.numel() * workspace.element_size(), _stream()), "dsa_forward")

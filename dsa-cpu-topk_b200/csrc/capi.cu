@@ -1,0 +1,192 @@
+// C ABI of libdsa_b200.so: argument checks, dispatch, per-thread error text,
+// and the whole-forward pipeline (stage 1 -> 2 -> 3) over caller workspace.
+#include <math.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "common.cuh"
+
+namespace dsa {
+
+// defined in the stage files
+int indexer_scores_simt(const void* q, const void* k, const float* w, float* scores, int64_t B,
+                        int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
+                        int dtype, int fill_upper, cudaStream_t stream);
+int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
+                      int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
+                      int fill_upper, cudaStream_t stream);
+bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype);
+int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
+                int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
+                int32_t* idx, int32_t* cnt, int64_t idx_cap, cudaStream_t stream);
+int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const float* scores,
+                const float* thr, const void* Q, const void* K, const void* V, float* O, int64_t B,
+                int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t DQ, int64_t DV,
+                float scale, int dtype, cudaStream_t stream);
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+void clear_error() { g_last_error.clear(); }
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(DSA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    return DSA_OK;
+}
+
+int num_sms() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+        return 148;
+    return n;
+}
+
+// kept-list capacity used by dsa_forward: k plus room for ties, multiple of 32
+int64_t idx_cap_for(int64_t k, int64_t T_k) {
+    int64_t cap = ((k + k / 4 + 32 + 31) / 32) * 32;
+    return cap < T_k ? cap : T_k;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct ForwardLayout {
+    size_t scores, thr, cnt, idx, total;
+    int64_t idx_cap;
+};
+
+static ForwardLayout forward_layout(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k) {
+    ForwardLayout L;
+    const int64_t rows = B * T_q;
+    const int64_t k = top_k < T_k ? top_k : T_k;
+    L.idx_cap = idx_cap_for(k, T_k);
+    size_t off = 0;
+    L.scores = off;
+    off += align256((size_t)rows * (size_t)T_k * sizeof(float));
+    L.thr = off;
+    off += align256((size_t)rows * sizeof(float));
+    L.cnt = off;
+    off += align256((size_t)rows * sizeof(int32_t));
+    L.idx = off;
+    off += align256((size_t)rows * (size_t)L.idx_cap * sizeof(int32_t));
+    L.total = off;
+    return L;
+}
+
+static int check_indexer_args(const void* q, const void* k, const float* w, const float* scores,
+                              int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI,
+                              int64_t DI, int dtype) {
+    if (!q || !k || !w || !scores) return fail(DSA_ERR_INVALID, "indexer_scores: null pointer");
+    if (B < 0 || T_q < 0 || T_k < 1 || q_row0 < 0 || HI < 1 || DI < 1)
+        return fail(DSA_ERR_INVALID, "indexer_scores: bad sizes");
+    if (HI > INT32_MAX || DI > INT32_MAX) return fail(DSA_ERR_INVALID, "indexer_scores: HI/DI too large");
+    if (!dtype_ok(dtype)) return fail(DSA_ERR_INVALID, "indexer_scores: unknown dtype");
+    return DSA_OK;
+}
+
+static int run_indexer(const void* q, const void* k, const float* w, float* scores, int64_t B,
+                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI, int dtype,
+                       int fill_upper, cudaStream_t st) {
+    if (indexer_tc_supported(HI, DI, dtype) && aligned16(q) && aligned16(k) && aligned16(scores) &&
+        aligned16(w))
+        return indexer_scores_tc(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, st);
+    return indexer_scores_simt(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper, st);
+}
+
+}  // namespace dsa
+
+using namespace dsa;
+
+extern "C" {
+
+int dsa_version(void) { return (0 << 16) | 1; }
+
+const char* dsa_last_error_string(void) { return g_last_error.c_str(); }
+
+int dsa_indexer_scores(const void* q, const void* k, const float* w, float* scores, int64_t B,
+                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
+                       int dtype, int fill_upper, void* stream) {
+    clear_error();
+    int rc = check_indexer_args(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype);
+    if (rc) return rc;
+    if (B * T_q == 0) return DSA_OK;
+    return run_indexer(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper,
+                       (cudaStream_t)stream);
+}
+
+int dsa_topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
+                    int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
+                    float* thr_out, int32_t* idx_out, int32_t* cnt_out, int64_t idx_cap,
+                    void* stream) {
+    clear_error();
+    return topk_select(scores, n_rows, row_len, row_stride, rows_per_batch, q_row0, causal, k,
+                       thr_out, idx_out, cnt_out, idx_cap, (cudaStream_t)stream);
+}
+
+int dsa_sparse_attn_threshold(const float* scores, const float* thr, const void* Q, const void* K,
+                              const void* V, float* O, int64_t B, int64_t T_q, int64_t T_k,
+                              int64_t q_row0, int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                              int dtype, void* stream) {
+    clear_error();
+    return sparse_attn(nullptr, nullptr, 0, scores, thr, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ,
+                       DV, scale, dtype, (cudaStream_t)stream);
+}
+
+int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const float* scores,
+                    const float* thr, const void* Q, const void* K, const void* V, float* O,
+                    int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t DQ,
+                    int64_t DV, float scale, int dtype, void* stream) {
+    clear_error();
+    if (!idx) return fail(DSA_ERR_INVALID, "sparse_attn: idx is required (use the threshold form)");
+    return sparse_attn(idx, cnt, idx_cap, scores, thr, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ, DV,
+                       scale, dtype, (cudaStream_t)stream);
+}
+
+size_t dsa_forward_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k) {
+    if (B < 0 || T_q < 0 || T_k < 1 || top_k < 1) return 0;
+    return forward_layout(B, T_q, T_k, top_k).total;
+}
+
+int dsa_forward(const void* q_idx, const void* k_idx, const float* w_idx, const void* Q,
+                const void* K, const void* V, float* O, int64_t B, int64_t T_q, int64_t T_k,
+                int64_t q_row0, int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV,
+                int64_t top_k, int idx_dtype, int qkv_dtype, void* workspace,
+                size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (top_k < 1) return fail(DSA_ERR_INVALID, "dsa_forward: top_k must be >= 1");
+    int rc = check_indexer_args(q_idx, k_idx, w_idx, O, B, T_q, T_k, q_row0, HI, DI, idx_dtype);
+    if (rc) return rc;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(DSA_ERR_INVALID, "dsa_forward: workspace must be non-null and 256-byte aligned");
+    const ForwardLayout L = forward_layout(B, T_q, T_k, top_k);
+    if (workspace_bytes < L.total)
+        return fail(DSA_ERR_INVALID, "dsa_forward: workspace too small (need " +
+                                         std::to_string(L.total) + " bytes)");
+    if (B * T_q == 0) return DSA_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    char* ws = static_cast<char*>(workspace);
+    float* scores = reinterpret_cast<float*>(ws + L.scores);
+    float* thr = reinterpret_cast<float*>(ws + L.thr);
+    int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt);
+    int32_t* idx = reinterpret_cast<int32_t*>(ws + L.idx);
+    const int64_t k = top_k < T_k ? top_k : T_k;
+
+    rc = run_indexer(q_idx, k_idx, w_idx, scores, B, T_q, T_k, q_row0, HI, DI, idx_dtype,
+                     /*fill_upper=*/0, st);
+    if (rc) return rc;
+    rc = topk_select(scores, B * T_q, T_k, T_k, T_q, q_row0, /*causal=*/1, k, thr, idx, cnt,
+                     L.idx_cap, st);
+    if (rc) return rc;
+    return sparse_attn(idx, cnt, L.idx_cap, scores, thr, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ,
+                       DV, 1.0f / sqrtf((float)DQ), qkv_dtype, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,85 @@
+// Shared helpers of the DSA B200 kernels: status reporting, element loads,
+// float <-> radix-key mapping.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/dsa_b200.h"
+
+namespace dsa {
+
+// ---- host-side status ----------------------------------------------------
+void set_error(const std::string& msg);
+void clear_error();
+int fail(int code, const std::string& msg);
+int check_launch(const char* what);
+int num_sms();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline size_t dtype_size(int dt) { return dt == DSA_F32 ? 4 : 2; }
+inline bool dtype_ok(int dt) { return dt == DSA_F32 || dt == DSA_BF16 || dt == DSA_F16; }
+
+// ---- device helpers --------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float to_f(float x) { return x; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+};
+template <> struct Elem<__half> {
+    static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+};
+
+// 16 bytes of T -> 16/sizeof(T) floats.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& v, float* out);
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& v, float* out) {
+    out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+    out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+template <>
+__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
+    // bf16 -> fp32 is a 16-bit left shift of the bit pattern.
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+template <>
+__device__ __forceinline__ void unpack16<__half>(const uint4& v, float* out) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        float2 f = __half22float2(h);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key).
+// -0.0 is folded onto +0.0 so that key equality matches float ==.
+__device__ __forceinline__ uint32_t f2key(float x) {
+    uint32_t b = __float_as_uint(x);
+    if ((b << 1) == 0) b = 0;  // +-0 -> +0
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(b);
+}
+
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+}  // namespace dsa

@@ -1,0 +1,117 @@
+"""DeepSeek Sparse Attention forward on B200 — drop-in for the reference module.
+
+Same public names, signatures and layouts as the reference's dsa_attention.py
+(Infatoshi/dsa-cpu-topk):
+
+    dsa_attention_triton(q_idx, k_idx, w_idx, Q, K, V, top_k, BLOCK_S=32)          :196-227
+    sparse_attention_with_threshold_triton(scores, threshold, Q, K, V)              :298-324
+    dsa_attention_split_triton(q_idx, k_idx, w_idx, Q, K, V, top_k, BLOCK_T=32, BLOCK_S=32) :327-344
+
+    q_idx [B,T,HI,DI]  k_idx [B,T,DI]  w_idx [B,T,HI]  Q/K [B,T,HQ,DQ]  V [B,T,HQ,DV]
+    -> O [B,T,HQ,DV] float32
+
+Semantics (dsa_attention.py:41-51): scores from the Lightning Indexer,
+threshold = k-th largest score of the row (k_eff = min(top_k, T)), keep every
+causal key with score >= threshold (ties kept), softmax(Q.K / sqrt(DQ)) over
+the kept keys, times V.
+
+Both reference entry points (the fused single kernel and the split
+pipeline) give the same result, so both run the same three-stage CUDA
+pipeline of libdsa_b200.so: tensor-core indexer -> radix-select top-K with
+kept-index lists -> gather attention with online softmax.  The reference's
+power-of-two and T <= ~512 limits are lifted; its other assertions
+(shapes, top_k <= T) are kept.  BLOCK_* arguments are accepted and ignored.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+import _native
+
+
+def _check_shapes(q_idx, k_idx, w_idx, Q, K, V):
+    assert q_idx.dim() == 4 and Q.dim() == 4 and K.dim() == 4 and V.dim() == 4
+    B, T, HQ, DQ = Q.shape
+    HI, DI = q_idx.shape[2], q_idx.shape[3]
+    assert q_idx.shape[:2] == (B, T) and k_idx.shape == (B, T, DI) and w_idx.shape == (B, T, HI)
+    assert K.shape == (B, T, HQ, DQ) and V.shape[:3] == (B, T, HQ)
+    assert all(t.is_cuda for t in (q_idx, k_idx, w_idx, Q, K, V)), "inputs must be CUDA tensors"
+
+
+def dsa_forward(q_idx, k_idx, w_idx, Q, K, V, top_k: int, *, q_row0: int = 0,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Whole DSA forward for query rows q_row0..q_row0+T_q-1.
+
+    q_idx [B,T_q,HI,DI], w_idx [B,T_q,HI], Q [B,T_q,HQ,DQ] hold those rows;
+    k_idx [B,T_k,DI], K [B,T_k,HQ,DQ], V [B,T_k,HQ,DV] hold keys 0..T_k-1.
+    ``workspace`` (uint8 CUDA tensor of forward_workspace_bytes(...) bytes) is
+    allocated when not given.  Returns O [B,T_q,HQ,DV] float32.
+    """
+    B, T_q = Q.shape[:2]
+    T_k = K.shape[1]
+    k_idx = k_idx.to(q_idx.dtype) if k_idx.dtype != q_idx.dtype else k_idx
+    K = K.to(Q.dtype) if K.dtype != Q.dtype else K
+    V = V.to(Q.dtype) if V.dtype != Q.dtype else V
+    q_idx, k_idx, Q, K, V = (_native.prep(t) for t in (q_idx, k_idx, Q, K, V))
+    w_idx = _native.prep(w_idx.float())
+    O = torch.empty((B, T_q, Q.shape[2], V.shape[3]), device=Q.device, dtype=torch.float32)
+    need = _native.forward_workspace_bytes(B, T_q, T_k, top_k)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, device=Q.device, dtype=torch.uint8)
+    _native.forward(q_idx, k_idx, w_idx, Q, K, V, O, top_k, workspace, q_row0=q_row0)
+    return O
+
+
+def forward_workspace_bytes(B: int, T_q: int, T_k: int, top_k: int) -> int:
+    return _native.forward_workspace_bytes(B, T_q, T_k, top_k)
+
+
+def dsa_attention_triton(q_idx, k_idx, w_idx, Q, K, V, top_k: int,
+                         BLOCK_S: int = 32) -> torch.Tensor:
+    _check_shapes(q_idx, k_idx, w_idx, Q, K, V)
+    assert top_k > 0 and top_k <= Q.shape[1], "top_k must be in [1, T]"
+    return dsa_forward(q_idx, k_idx, w_idx, Q, K, V, top_k)
+
+
+def dsa_attention_split_triton(q_idx, k_idx, w_idx, Q, K, V, top_k: int,
+                               BLOCK_T: int = 32, BLOCK_S: int = 32) -> torch.Tensor:
+    _check_shapes(q_idx, k_idx, w_idx, Q, K, V)
+    assert top_k > 0 and top_k <= Q.shape[1], "top_k must be in [1, T]"
+    return dsa_forward(q_idx, k_idx, w_idx, Q, K, V, top_k)
+
+
+def sparse_attention_with_threshold_triton(scores, threshold, Q, K, V) -> torch.Tensor:
+    """Attention over keys s <= t with scores[b,t,s] >= threshold[b,t] (dsa_attention.py:298-324)."""
+    B, T, _ = scores.shape
+    HQ, DQ = Q.shape[-2], Q.shape[-1]
+    DV = V.shape[-1]
+    assert Q.shape[:2] == (B, T) and K.shape[:2] == (B, T) and V.shape[:2] == (B, T)
+    assert threshold.numel() == B * T
+    K = K.to(Q.dtype) if K.dtype != Q.dtype else K
+    V = V.to(Q.dtype) if V.dtype != Q.dtype else V
+    scores = _native.prep(scores.float())
+    threshold = _native.prep(threshold.float())
+    Q, K, V = _native.prep(Q), _native.prep(K), _native.prep(V)
+    out = torch.empty(B, T, HQ, DV, device=Q.device, dtype=torch.float32)
+    _native.sparse_attn_threshold(scores, threshold, Q, K, V, out, scale=1.0 / math.sqrt(DQ))
+    return out
+
+
+def sparse_attention_with_lists(idx, cnt, idx_cap, scores, threshold, Q, K, V, *,
+                                q_row0: int = 0) -> torch.Tensor:
+    """Attention over the kept-index lists of topk.topk_select (list form of stage 3).
+
+    Rows whose cnt exceeds idx_cap are recomputed from scores/threshold, so
+    those must be given unless idx_cap covers every row.
+    """
+    B, T_q, HQ, DQ = Q.shape
+    DV = V.shape[-1]
+    Q, K, V = _native.prep(Q), _native.prep(K), _native.prep(V)
+    out = torch.empty(B, T_q, HQ, DV, device=Q.device, dtype=torch.float32)
+    _native.sparse_attn(_native.prep(idx), _native.prep(cnt), idx_cap,
+                        None if scores is None else _native.prep(scores.float()),
+                        None if threshold is None else _native.prep(threshold.float()),
+                        Q, K, V, out, q_row0=q_row0, scale=1.0 / math.sqrt(DQ))
+    return out

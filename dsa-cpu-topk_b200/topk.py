@@ -1,0 +1,71 @@
+"""Per-row top-K threshold / kept-index selection on the GPU (stage 2).
+
+GPU replacement of the reference's top-K code paths:
+
+    topk_threshold(scores, k)              topk_avx512.cpp:251-253 (ext.topk_threshold)
+    topk_threshold_batch_merge(scores, k)  topk_avx512.cpp:255-257 (same result, other CPU strategy)
+    select_threshold(scores, top_k)        dsa_attention.py:41-44 / :343-344 (topk(...).values[..., -1:])
+    topk_select(scores, k, ...)            threshold + ascending kept-index list + count
+
+All run the radix-select kernel of libdsa_b200.so on the current stream; the
+threshold equals torch.topk(scores, k).values[..., k-1] by value (-0.0 and
++0.0 are the same value), and the kept set is {s : scores[s] >= thr}
+(ties kept), restricted to s <= t for causal rows.
+"""
+from __future__ import annotations
+
+import torch
+
+import _native
+
+
+def idx_cap_for(k: int, row_len: int) -> int:
+    """List capacity used by the forward: k plus room for ties, multiple of 32."""
+    return min(row_len, ((k + k // 4 + 32 + 31) // 32) * 32)
+
+
+def topk_select(scores: torch.Tensor, k: int, *, causal: bool = False, q_row0: int = 0,
+                idx_cap: int | None = None, return_idx: bool = True):
+    """scores [..., N] fp32 CUDA -> (thr [rows], idx [rows, idx_cap] int32, cnt [rows] int32).
+
+    With ``causal`` the tensor must be [B, T_q, N]: row t (absolute position
+    q_row0 + t) keeps only s <= t and entries s > t count as -inf.  Entries of
+    idx past cnt (or all of it when return_idx is False) are unspecified /
+    None.  cnt can exceed idx_cap when many values tie; then the list holds
+    the first idx_cap kept positions.
+    """
+    assert scores.is_cuda and scores.dtype == torch.float32, "scores must be fp32 CUDA"
+    N = scores.shape[-1]
+    assert 1 <= k <= N, f"need 1 <= k <= N (k={k}, N={N})"
+    s = _native.prep(scores)
+    rows = s.numel() // N
+    rows_per_batch = s.shape[-2] if (causal and s.dim() >= 2) else 1
+    thr = torch.empty(rows, device=s.device, dtype=torch.float32)
+    if not return_idx:
+        _native.topk_select(s, rows, N, N, k, thr, causal=causal, rows_per_batch=rows_per_batch,
+                            q_row0=q_row0)
+        return thr, None, None
+    cap = N if idx_cap is None else idx_cap
+    idx = torch.empty((rows, cap), device=s.device, dtype=torch.int32)
+    cnt = torch.empty(rows, device=s.device, dtype=torch.int32)
+    _native.topk_select(s, rows, N, N, k, thr, idx, cnt, cap, causal=causal,
+                        rows_per_batch=rows_per_batch, q_row0=q_row0)
+    return thr, idx, cnt
+
+
+def topk_threshold(scores: torch.Tensor, k: int) -> torch.Tensor:
+    """[..., N] fp32 -> [..., 1] k-th largest per row (topk_avx512.cpp:226-253 contract)."""
+    assert k > 0, "k must be > 0"
+    assert k <= scores.shape[-1], "k must be <= N"
+    thr, _, _ = topk_select(scores, k, return_idx=False)
+    return thr.view(*scores.shape[:-1], 1)
+
+
+def topk_threshold_batch_merge(scores: torch.Tensor, k: int) -> torch.Tensor:
+    """Same result as topk_threshold (the reference's second CPU strategy)."""
+    return topk_threshold(scores, k)
+
+
+def select_threshold(scores: torch.Tensor, top_k: int) -> torch.Tensor:
+    """dsa_attention.py:41-44: k_eff = min(top_k, N); returns thr [..., 1]."""
+    return topk_threshold(scores, min(top_k, scores.shape[-1]))

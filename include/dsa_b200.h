@@ -1,0 +1,147 @@
+/*
+ * dsa_b200.h — C ABI of the B200 DeepSeek Sparse Attention forward.
+ *
+ * Three sm_100a CUDA stages behind plain pointers and sizes:
+ *   stage 1  Lightning Indexer scores   I[b,t,s] = sum_j w[b,t,j] * ReLU(<q[b,t,j,:], k[b,s,:]>)
+ *   stage 2  per-row top-K threshold (k-th largest) + kept-index list (keep ties)
+ *   stage 3  sparse attention over the kept keys (online softmax)
+ *
+ * Conventions shared by every entry point
+ *   - All pointers are device pointers on the current CUDA device, row-major
+ *     and contiguous in the layouts given below, 16-byte aligned.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Every call only enqueues work: nothing synchronises, nothing allocates.
+ *     The caller owns every buffer, outputs and workspaces included.
+ *   - Returns DSA_OK (0) or a negative dsa_status.  On error,
+ *     dsa_last_error_string() (per host thread) describes the failure.
+ *   - Query rows: a call covers T_q query rows of each batch whose absolute
+ *     positions are q_row0 .. q_row0+T_q-1 (so a GPU can own a block of
+ *     rows of a longer sequence), against T_k key positions 0..T_k-1.  Key s
+ *     is causal for query t iff s <= t.
+ *   - dtype codes: DSA_F32, DSA_BF16, DSA_F16 (element type of the named
+ *     tensors; everything else is fp32 / int32 as stated).
+ *
+ * Reference interfaces replaced (Infatoshi/dsa-cpu-topk, file:line):
+ *   dsa_indexer_scores         lightning_indexer.py:100-125  indexer_scores_triton / _indexer_score_kernel
+ *   dsa_topk_select            dsa_attention.py:343-344      scores.topk(k)[..., -1:] on the GPU, and
+ *                              topk_avx512.cpp:226-257       topk_threshold / topk_threshold_batch_merge
+ *   dsa_sparse_attn_threshold  dsa_attention.py:298-324      sparse_attention_with_threshold_triton
+ *   dsa_sparse_attn            dsa_attention.py:72-87        (gather form of the selection, naive variant)
+ *   dsa_forward                dsa_attention.py:327-344      dsa_attention_split_triton (and the fused
+ *                              dsa_attention.py:196-227      dsa_attention_triton, same result)
+ */
+#ifndef DSA_B200_H
+#define DSA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSA_API __attribute__((visibility("default")))
+#else
+#define DSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    DSA_OK = 0,
+    DSA_ERR_INVALID = -1,      /* bad shape, pointer, alignment or argument */
+    DSA_ERR_UNSUPPORTED = -2,  /* valid request this build cannot run (e.g. dtype) */
+    DSA_ERR_CUDA = -3          /* a CUDA runtime call failed (launch, attribute) */
+} dsa_status;
+
+typedef enum { DSA_F32 = 0, DSA_BF16 = 1, DSA_F16 = 2 } dsa_dtype;
+
+/* Library version, (major << 16) | minor. */
+DSA_API int dsa_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+DSA_API const char* dsa_last_error_string(void);
+
+/*
+ * Stage 1 — Lightning Indexer scores.
+ *   q       [B, T_q, HI, DI]  dtype      indexer queries of rows q_row0..q_row0+T_q-1
+ *   k       [B, T_k, DI]      dtype      shared indexer key
+ *   w       [B, T_q, HI]      fp32       per-query head weights
+ *   scores  [B, T_q, T_k]     fp32 out   score of causal entries; entries s > t are
+ *                                        written -inf when fill_upper != 0, else left
+ *                                        untouched or -inf (stages 2/3 never read them)
+ * dtype DSA_BF16 with DI % 16 == 0 runs on the tcgen05 tensor cores; other
+ * shapes and DSA_F32 run the fp32 CUDA-core kernel (IEEE fp32 products and sums).
+ * Replaces lightning_indexer.py:100-125 (which requires DI a power of two).
+ */
+DSA_API int dsa_indexer_scores(const void* q, const void* k, const float* w, float* scores,
+                       int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                       int64_t HI, int64_t DI, int dtype, int fill_upper, void* stream);
+
+/*
+ * Stage 2 — per-row top-K threshold and kept-index list (radix select).
+ *   scores   n_rows rows of row_len fp32, row r at scores + r*row_stride
+ *   thr_out  [n_rows] fp32 out: the k-th largest value of the row (as
+ *            torch.topk(k).values[..., k-1]; -0.0 and +0.0 are one value)
+ *   idx_out  [n_rows, idx_cap] int32 out (may be NULL): ascending positions s
+ *            with scores[s] >= thr (and s <= t when causal); at most idx_cap written
+ *   cnt_out  [n_rows] int32 out (may be NULL): number of kept positions, which
+ *            can exceed k (ties are kept) and idx_cap (then the list is truncated)
+ * causal != 0: row r is query t = q_row0 + r % rows_per_batch and entries
+ * s > t count as -inf whatever is stored there (they are not read).
+ * Requires 1 <= k <= row_len.
+ */
+DSA_API int dsa_topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
+                    int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
+                    float* thr_out, int32_t* idx_out, int32_t* cnt_out, int64_t idx_cap,
+                    void* stream);
+
+/*
+ * Stage 3 (threshold form) — attention of each query over the keys s <= t
+ * with scores[s] >= thr[row].
+ *   scores [B, T_q, T_k] fp32 (row stride T_k), thr [B*T_q] fp32
+ *   Q [B, T_q, HQ, DQ], K [B, T_k, HQ, DQ], V [B, T_k, HQ, DV]   dtype
+ *   O [B, T_q, HQ, DV] fp32 out
+ * scale multiplies the logits (the reference uses 1/sqrt(DQ)).
+ */
+DSA_API int dsa_sparse_attn_threshold(const float* scores, const float* thr,
+                              const void* Q, const void* K, const void* V, float* O,
+                              int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                              int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                              int dtype, void* stream);
+
+/*
+ * Stage 3 (list form) — attention over the index lists of dsa_topk_select.
+ *   idx [B*T_q, idx_cap] int32, cnt [B*T_q] int32
+ * Rows whose cnt exceeds idx_cap fall back to the threshold form, so scores
+ * and thr (as above) must be given whenever idx_cap < min(T_k, q_row0+T_q);
+ * otherwise they may be NULL.
+ */
+DSA_API int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap,
+                    const float* scores, const float* thr,
+                    const void* Q, const void* K, const void* V, float* O,
+                    int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                    int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                    int dtype, void* stream);
+
+/*
+ * Whole forward (stage 1 -> 2 -> 3) in caller-provided workspace.
+ * idx_dtype is the dtype of q_idx/k_idx, qkv_dtype that of Q/K/V; w_idx is fp32.
+ * Layouts as above: q_idx [B,T_q,HI,DI], k_idx [B,T_k,DI], w_idx [B,T_q,HI],
+ * Q [B,T_q,HQ,DQ], K [B,T_k,HQ,DQ], V [B,T_k,HQ,DV], O [B,T_q,HQ,DV] fp32.
+ * top_k is clamped to T_k (k_eff = min(k, T), dsa_attention.py:41).
+ * workspace must hold dsa_forward_workspace_bytes(...) bytes, 256-byte aligned.
+ */
+DSA_API size_t dsa_forward_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k);
+
+DSA_API int dsa_forward(const void* q_idx, const void* k_idx, const float* w_idx,
+                const void* Q, const void* K, const void* V, float* O,
+                int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV, int64_t top_k,
+                int idx_dtype, int qkv_dtype, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H */

@@ -1,0 +1,113 @@
+"""GPU: the whole DSA forward and the attention stage against the oracle.
+
+Tolerances: abs 5e-4 on the reference tests' small cases (test_dsa.py:41,61);
+rtol 1e-3 fp32 / 2e-2 bf16 elsewhere (north-star parity bar)."""
+import glob
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden, t
+import dsa_oracle as o
+
+pytestmark = pytest.mark.gpu
+
+NAMES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "dsa_*.npz")))
+
+
+def inputs(d, cuda):
+    dt = torch.bfloat16 if str(d["dtype"]) == "bfloat16" else torch.float32
+    return [t(d["q_idx"], cuda, dt), t(d["k_idx"], cuda, dt), t(d["w_idx"], cuda),
+            t(d["Q"], cuda, dt), t(d["K"], cuda, dt), t(d["V"], cuda, dt)], dt
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_forward_matches_reference_golden(cuda, name):
+    from dsa_attention import dsa_attention_split_triton, dsa_attention_triton
+    from dsa_hybrid import HybridContext, dsa_hybrid_cpu_topk
+    d = golden(name)
+    args, dt = inputs(d, cuda)
+    k = int(d["top_k"])
+    ref = t(d["out"])
+    tol = 5e-4 if dt == torch.float32 else 2e-2
+    for fn in (dsa_attention_split_triton, dsa_attention_triton):
+        out = fn(*args, top_k=k).cpu()
+        assert out.dtype == torch.float32 and out.shape == ref.shape
+        assert (out - ref).abs().max() < tol, fn.__name__
+    ctx = HybridContext(*args[3].shape[:2])
+    out = dsa_hybrid_cpu_topk(*args, top_k=k, ctx=ctx).cpu()
+    assert (out - ref).abs().max() < tol
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_threshold_form_matches_oracle(cuda, name):
+    """Stage 3 alone on the reference's own scores and thresholds."""
+    from dsa_attention import sparse_attention_with_threshold_triton
+    d = golden(name)
+    args, dt = inputs(d, cuda)
+    sc = o.indexer_scores(*(a.cpu() for a in args[:3]))
+    thr = t(d["thr"])
+    out = sparse_attention_with_threshold_triton(sc.to(cuda), thr.to(cuda), *args[3:]).cpu()
+    ref = o.sparse_attention_with_threshold(sc, thr, *(a.cpu() for a in args[3:]))
+    assert (out - ref).abs().max() < (1e-4 if dt == torch.float32 else 1e-3)
+
+
+def test_list_form_overflow_rows_fall_back(cuda):
+    """Rows whose kept count overflows the list are recomputed from the scores."""
+    from dsa_attention import sparse_attention_with_lists
+    from topk import topk_select
+    B, T, H, D = 2, 200, 4, 32
+    _, _, _, Q, K, V = o.make_inputs(B, T, 1, 8, H, D, D)
+    sc = torch.round(torch.randn(B, T, T, generator=torch.Generator().manual_seed(1)))  # many ties
+    sc = sc.masked_fill(~torch.ones(T, T, dtype=torch.bool).tril(), float("-inf"))
+    thr, idx, cnt = topk_select(sc.to(cuda), 16, causal=True, idx_cap=32)
+    assert (cnt > 32).any()
+    out = sparse_attention_with_lists(idx, cnt, 32, sc.to(cuda), thr, Q.to(cuda), K.to(cuda), V.to(cuda)).cpu()
+    ref = o.sparse_attention_with_threshold(sc, thr.cpu().view(B, T, 1), Q, K, V)
+    assert (out - ref).abs().max() < 1e-4
+
+
+@pytest.mark.parametrize("B,T,HI,DI,HQ,D,k,dtype", [
+    (16, 512, 4, 32, 4, 32, 32, torch.float32),    # config c1
+    (4, 512, 4, 32, 4, 32, 128, torch.float32),    # config c3 corner
+    (1, 1000, 8, 64, 8, 64, 100, torch.bfloat16),  # ragged bf16
+    (1, 2048, 16, 64, 16, 64, 512, torch.bfloat16),  # c4 head shapes, shorter T
+    (3, 77, 2, 16, 2, 16, 80, torch.float32),      # k > T: every causal key kept
+    (1, 300, 4, 32, 2, 128, 16, torch.float32),    # D = 128 fp32
+    (1, 300, 4, 32, 8, 256, 16, torch.bfloat16),   # D = 256 bf16 (1024-thread rows)
+])
+def test_forward_random(cuda, B, T, HI, DI, HQ, D, k, dtype):
+    """End to end against the oracle, with the selection checked on the GPU's own scores."""
+    from dsa_attention import dsa_forward
+    from lightning_indexer import indexer_scores
+    from topk import topk_select
+    qi, ki, wi, Q, K, V = o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype)
+    dev = [x.to(cuda) for x in (qi, ki, wi, Q, K, V)]
+    out = dsa_forward(*dev, min(k, T)).cpu()
+    # the GPU's own scores -> oracle selection -> oracle attention
+    sc = indexer_scores(*dev[:3]).cpu()
+    kk = min(k, T)
+    thr, idx, cnt = topk_select(sc.to(cuda), kk, causal=True)
+    othr, oidx, ocnt = o.topk_select(sc, kk, causal=True, rows_per_batch=T)
+    assert np.array_equal(thr.cpu().numpy(), othr) and np.array_equal(cnt.cpu().numpy(), ocnt)
+    ref = o.sparse_attention_with_threshold(sc, torch.from_numpy(othr).view(B, T, 1), Q, K, V)
+    rtol = 1e-3 if dtype == torch.float32 else 2e-2
+    err = (out - ref).abs()
+    assert bool((err <= 1e-4 + rtol * ref.abs()).all()), f"max err {err.max().item()}"
+    # and against the fully independent oracle (its own fp32 scores)
+    ref2 = o.dsa_attention(qi, ki, wi, Q, K, V, k)
+    bad = ((out - ref2).abs() > 1e-3 + rtol * ref2.abs()).any(-1).any(-1)
+    assert bad.float().mean() < 0.002, "rows differing from the independent oracle"
+
+
+def test_row_sharded_forward_equals_whole(cuda):
+    """q_row0 offsets: computing row blocks separately gives the same output."""
+    from dsa_attention import dsa_forward
+    qi, ki, wi, Q, K, V = (x.to(cuda) for x in o.make_inputs(2, 640, 4, 32, 4, 32, 32))
+    whole = dsa_forward(qi, ki, wi, Q, K, V, 64)
+    parts = [dsa_forward(qi[:, a:b], ki, wi[:, a:b], Q[:, a:b], K, V, 64, q_row0=a)
+             for a, b in [(0, 100), (100, 333), (333, 640)]]
+    assert torch.equal(torch.cat(parts, 1), whole)
