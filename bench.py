@@ -1,0 +1,525 @@
+"""DSA forward benchmark: query-tokens/s on 1..8 B200s, with per-stage rooflines.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+A step is one DSA forward (indexer -> top-K -> sparse attention) over one
+batch of the workload, run through the C ABI of libdsa_b200.so.  Default
+workload: config c5 (DeepSeek-V3.2 scale, B=1 T=32768 HI=64 DI=128 HQ=16
+D=128 k=2048, bf16), the largest configuration that fits one GPU.
+
+Scaling: "weak" (default) gives every rank its own sequences (batch
+sharding); "strong" splits one workload's query rows across ranks (zig-zag
+row blocks).  Neither communicates on the hot path.  Timing: W untimed
+steps, then K steps between barrier + synchronize, CUDA events on the
+launching stream, max over ranks.  Inputs are larger than L2 (c5: 0.9 GB of
+inputs and a 4.3 GB score matrix per step), so no L2 flush is needed.
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference's
+own CPU path (torch variant + the reference's AVX-512 top-K built in
+oracle/_ref) on a bounded sample of the same workload's rows.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "dsa-cpu-topk_b200"))
+
+CONFIGS = {
+    # name: B, T, HI, DI, HQ, DQ(=DV), top_k, dtype, description
+    "c1": dict(B=16, T=512, HI=4, DI=32, HQ=4, D=32, k=32, dtype="f32",
+               desc="DSA fwd B16 T512 k32 HI4 DI32 HQ4 D32 fp32, causal"),
+    "c3_b64_k128": dict(B=64, T=512, HI=4, DI=32, HQ=4, D=32, k=128, dtype="f32",
+                        desc="DSA fwd B64 T512 k128 HI4 DI32 HQ4 D32 fp32, causal (c3 sweep corner)"),
+    "c4": dict(B=4, T=8192, HI=16, DI=64, HQ=16, D=64, k=512, dtype="bf16",
+               desc="DSA fwd B4 T8192 k512 HI16 DI64 HQ16 D64 bf16, causal"),
+    "c5": dict(B=1, T=32768, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16",
+               desc="DSA fwd B1 T32768 k2048 HI64 DI128 HQ16 D128 bf16, causal (DeepSeek-V3.2 scale)"),
+}
+DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes from committed ncu summaries (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.gpu = vis.split(",")[local_rank] if vis else str(local_rank)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                c = [x.strip() for x in line.split(",")]
+                if len(c) < 9:
+                    continue
+                try:
+                    sm.append(float(c[1].split()[0]))
+                    mx.append(float(c[2].split()[0]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, c[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------------------
+# workload
+# --------------------------------------------------------------------------
+
+def make_inputs_device(cfg, B, dev, seed):
+    """Seeded synthetic inputs of the config's shapes (N(0,1); w ~ N(0,1)/sqrt(HI))."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    dt = DT[cfg["dtype"]]
+    T, HI, DI, HQ, D = cfg["T"], cfg["HI"], cfg["DI"], cfg["HQ"], cfg["D"]
+
+    def rnd(shape, scale=1.0, dtype=dt):
+        return (torch.randn(shape, generator=g, device=dev) * scale).to(dtype)
+
+    return (rnd((B, T, HI, DI)), rnd((B, T, DI)), rnd((B, T, HI), 1 / math.sqrt(HI), torch.float32),
+            rnd((B, T, HQ, D)), rnd((B, T, HQ, D)), rnd((B, T, HQ, D)))
+
+
+class Pipeline:
+    """Preallocated buffers and the three C-ABI stage calls for some row blocks."""
+
+    def __init__(self, inputs, blocks, k):
+        import _native
+        from topk import idx_cap_for
+        self.n = _native
+        q, kk, w, Q, K, V = inputs
+        self.k_idx, self.K, self.V = kk, K, V
+        B, T = Q.shape[:2]
+        self.k = min(k, T)
+        self.cap = idx_cap_for(self.k, T)
+        self.parts = []
+        dev = Q.device
+        for blk in blocks:
+            Tq = blk.stop - blk.start
+            sl = slice(blk.start, blk.stop)
+            p = dict(q0=blk.start, Tq=Tq, q=q[:, sl].contiguous(), w=w[:, sl].contiguous(),
+                     Q=Q[:, sl].contiguous(),
+                     scores=torch.empty((B, Tq, T), device=dev, dtype=torch.float32),
+                     thr=torch.empty(B * Tq, device=dev, dtype=torch.float32),
+                     cnt=torch.empty(B * Tq, device=dev, dtype=torch.int32),
+                     idx=torch.empty((B * Tq, self.cap), device=dev, dtype=torch.int32),
+                     O=torch.empty((B, Tq, Q.shape[2], V.shape[3]), device=dev, dtype=torch.float32))
+            self.parts.append(p)
+        self.launches_per_step = 3 * len(self.parts)
+
+    def step(self, ev=None):
+        n = self.n
+        for i, p in enumerate(self.parts):
+            if ev is not None:
+                ev[i][0].record()
+            n.indexer_scores(p["q"], self.k_idx, p["w"], p["scores"], q_row0=p["q0"], fill_upper=False)
+            if ev is not None:
+                ev[i][1].record()
+            B, Tq, T = p["scores"].shape
+            n.topk_select(p["scores"], B * Tq, T, T, self.k, p["thr"], p["idx"], p["cnt"], self.cap,
+                          causal=True, rows_per_batch=Tq, q_row0=p["q0"])
+            if ev is not None:
+                ev[i][2].record()
+            n.sparse_attn(p["idx"], p["cnt"], self.cap, p["scores"], p["thr"], p["Q"], self.K, self.V,
+                          p["O"], q_row0=p["q0"])
+            if ev is not None:
+                ev[i][3].record()
+
+    def algorithmic(self, cfg):
+        """Per-step algorithmic work of each stage (from the actual kept counts)."""
+        elt = 2 if cfg["dtype"] == "bf16" else 4
+        HI, DI, HQ, D = cfg["HI"], cfg["DI"], cfg["HQ"], cfg["D"]
+        flops = topk_b = attn_b = attn_f = 0
+        for p in self.parts:
+            B, Tq, T = p["scores"].shape
+            t = torch.arange(p["q0"], p["q0"] + Tq, dtype=torch.float64)
+            valid = torch.clamp(t + 1, max=T).sum().item() * B
+            sel = p["cnt"].double().sum().item()
+            rows = B * Tq
+            flops += 2.0 * HI * DI * valid
+            topk_b += 4.0 * valid + 8.0 * rows + 4.0 * sel
+            attn_b += sel * HQ * 2 * D * elt + rows * HQ * D * (elt + 4) + 4.0 * sel + 4.0 * rows
+            attn_f += sel * HQ * 4.0 * D
+        return dict(indexer_flops=flops, topk_bytes=topk_b, attn_bytes=attn_b, attn_flops=attn_f)
+
+
+# --------------------------------------------------------------------------
+# the reference's CPU path (timed baseline; oracle/ is used only here)
+# --------------------------------------------------------------------------
+
+def cpu_reference_setup(cfg, inputs):
+    """Host copies of one sequence (batch 0) and the reference's compiled top-K."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import build_ref
+    import dsa_oracle
+    ext = build_ref.load_ref()
+    host = [x[:1].float().cpu() for x in inputs]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    return dict(ext=ext, oracle=dsa_oracle, host=host, threads=threads)
+
+
+def cpu_reference_rows(ctx, cfg, rows: range):
+    """The reference torch variant's work for query rows ``rows`` of one sequence:
+    dense indexer einsum over all T keys (lightning_indexer.py:26-33), k-th
+    largest per row (the reference's AVX-512 topk_threshold, else torch.topk)
+    and the dense masked softmax attention (dsa_attention.py:46-51)."""
+    o = ctx["oracle"]
+    q, kk, w, Q, K, V = ctx["host"]
+    a, z = rows.start, rows.stop
+    s = o.indexer_scores(q, kk, w, slice(a, z))
+    k_eff = min(cfg["k"], s.shape[-1])
+    thr = ctx["ext"].topk_threshold(s.contiguous(), k_eff) if ctx["ext"] is not None \
+        else o.select_threshold(s, k_eff)
+    return o._attend(s, thr, Q, K, V, a, z, 1.0 / math.sqrt(cfg["D"]))
+
+
+def cpu_reference_rate(ctx, cfg, seconds: float, chunk: int):
+    """Query rows/s of the reference CPU path over a bounded sample of rows
+    spread across the sequence (the torch variant's cost per row does not
+    depend on t: it scores every key and masks)."""
+    T = cfg["T"]
+    starts = list(range(0, T - chunk + 1, max(chunk, (T // 64) // chunk * chunk or chunk)))
+    cpu_reference_rows(ctx, cfg, range(starts[0], starts[0] + chunk))    # warm-up
+    done, t0 = 0, time.perf_counter()
+    i = 0
+    while True:
+        a = starts[(i * 37) % len(starts)]
+        cpu_reference_rows(ctx, cfg, range(a, a + chunk))
+        done += chunk
+        i += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= T * cfg["B"]:
+            return done / el, done, el
+
+
+def cpu_kind(ctx):
+    return "reference" if ctx["ext"] is not None else "port"
+
+
+def cpu_sample_text(ctx, cfg, rows, el):
+    topk = ("the reference's topk_avx512.cpp built from its sources in oracle/_ref"
+            if ctx["ext"] is not None else "torch.topk (AVX-512 extension unavailable on this host)")
+    return (f"{rows} query rows of {cfg['desc']} in {el:.1f} s; dense indexer + masked softmax as "
+            f"the reference torch variant (restated in oracle/dsa_oracle.py, fp32 upcast), top-K by {topk}; "
+            f"OMP/torch threads={ctx['threads']}")
+
+
+CHUNK = {"c1": 512, "c3_b64_k128": 512, "c4": 64, "c5": 16}
+
+
+# --------------------------------------------------------------------------
+# arms
+# --------------------------------------------------------------------------
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def base_line(args, cfg, world, value, ms, unit="query-tokens/s"):
+    B_glob = cfg["B"] * (world if args.scaling == "weak" else 1)
+    return {
+        "metric": "DSA fwd query-tokens/s",
+        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1) inputs of the config's shapes)",
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "global_batch": B_glob,
+                   "seq_len": cfg["T"], "top_k": cfg["k"], "HI": cfg["HI"], "DI": cfg["DI"],
+                   "HQ": cfg["HQ"], "D": cfg["D"],
+                   "parallelism": (f"batch-shard x{world}" if args.scaling == "weak"
+                                   else f"query-row zig-zag x{world}"),
+                   "l2": "inputs larger than L2" if cfg["T"] >= 8192 else
+                         "L2 flushed between steps (256 MB write)"},
+    }
+
+
+def run_b200(args, cfg, world, rank, local):
+    import sharding
+    from dsa_attention import dsa_forward, forward_workspace_bytes
+    dev = torch.device("cuda", local)
+    B, T = cfg["B"], cfg["T"]
+    seed = 1000 * (rank if args.scaling == "weak" else 0)
+    inputs = make_inputs_device(cfg, B, dev, seed)
+    if args.scaling == "weak":
+        blocks = [sharding.RowBlock(0, T)]
+    else:
+        blocks = sharding.zigzag_plan(T, world)[rank]
+    pipe = Pipeline(inputs, blocks, cfg["k"])
+    flush = None if T >= 8192 else torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        pipe.step()
+    nb = len(pipe.parts)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nb)]
+           for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total_ms = 0.0
+    if flush is None:
+        start.record(stream)
+        for s in range(args.steps):
+            pipe.step(evs[s])
+        end.record(stream)
+        barrier(world)
+        total_ms = start.elapsed_time(end)
+    else:
+        # small workloads: flush L2 between steps, time only the steps
+        for s in range(args.steps):
+            flush.zero_()
+            start.record(stream)
+            pipe.step(evs[s])
+            end.record(stream)
+            end.synchronize()
+            total_ms += start.elapsed_time(end)
+        barrier(world)
+    clk = clocks.stop()
+    stage_ms = [0.0, 0.0, 0.0]
+    for s in range(args.steps):
+        for i in range(nb):
+            for j in range(3):
+                stage_ms[j] += evs[s][i][j].elapsed_time(evs[s][i][j + 1])
+    stage_ms = [x / args.steps for x in stage_ms]
+    t_max = max_over_ranks(total_ms, world)
+    ms = t_max / args.steps
+    tokens = B * T * (world if args.scaling == "weak" else 1)
+    value = tokens / (ms / 1e3)
+
+    # rooflines of each stage (algorithmic work / measured average duration)
+    hbm, tflops, src = load_peaks()
+    peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if src == "measured" else {}
+    tf_sust = peaks.get("bf16_tflops_sustained", 1390.7 if src == "fallback" else tflops)
+    alg = pipe.algorithmic(cfg)
+    traffic = load_traffic().get(args.config, {})
+    stages = {
+        "indexer": dict(bound="tensor", achieved=alg["indexer_flops"] / (stage_ms[0] / 1e3) / 1e12,
+                        peak=tf_sust, unit="TFLOP/s", ms=stage_ms[0],
+                        kernel="indexer_tc" if cfg["dtype"] == "bf16" else "indexer_simt (fp32 CUDA cores)",
+                        traffic=traffic.get("indexer")),
+        "topk": dict(bound="hbm", achieved=alg["topk_bytes"] / (stage_ms[1] / 1e3) / 1e9, peak=hbm,
+                     unit="GB/s", ms=stage_ms[1], kernel="topk_select_kernel", traffic=traffic.get("topk")),
+        "sparse_attn": dict(bound="hbm", achieved=alg["attn_bytes"] / (stage_ms[2] / 1e3) / 1e9, peak=hbm,
+                            unit="GB/s", ms=stage_ms[2], kernel="sparse_attn_kernel",
+                            traffic=traffic.get("sparse_attn")),
+    }
+    for v in stages.values():
+        v["frac"] = v["achieved"] / v["peak"]
+        v["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
+    top = max(stages, key=lambda n: stages[n]["ms"])
+    roof = {k2: stages[top][k2] for k2 in ("bound", "achieved", "peak", "unit", "frac", "traffic")}
+    roof["kernel"] = top
+
+    line = base_line(args, cfg, world, value, ms)
+    line["roofline"] = roof
+    line["stages"] = stages
+    line["algorithmic"] = alg
+    line["clocks"] = clk
+    line["gpu_launches"] = pipe.launches_per_step * args.steps
+
+    # ---- end to end through the public API: pinned host inputs -> device -> O back to host
+    if not args.no_e2e:
+        q, kk, w, Q, K, V = inputs
+        h_key = [x.cpu().pin_memory() for x in (kk, K, V)]
+        h_rows = [[x[:, b.start:b.stop].cpu().pin_memory() for x in (q, w, Q)] for b in blocks]
+        d_key = [torch.empty_like(x, device=dev) for x in h_key]
+        d_rows = [[torch.empty_like(x, device=dev) for x in r] for r in h_rows]
+        ws = [torch.empty(forward_workspace_bytes(B, b.stop - b.start, T, cfg["k"]), device=dev,
+                          dtype=torch.uint8) for b in blocks]
+        h_out = [torch.empty((B, b.stop - b.start, cfg["HQ"], cfg["D"]), dtype=torch.float32).pin_memory()
+                 for b in blocks]
+        bi = sum(x.numel() * x.element_size() for x in h_key) + \
+            sum(x.numel() * x.element_size() for r in h_rows for x in r)
+        bo = sum(x.numel() * x.element_size() for x in h_out)
+
+        def e2e_step():
+            for d, h in zip(d_key, h_key):
+                d.copy_(h, non_blocking=True)
+            for dr, hr in zip(d_rows, h_rows):
+                for d, h in zip(dr, hr):
+                    d.copy_(h, non_blocking=True)
+            for i, b in enumerate(blocks):
+                out = dsa_forward(d_rows[i][0], d_key[0], d_rows[i][1], d_rows[i][2], d_key[1], d_key[2],
+                                  cfg["k"], q_row0=b.start, workspace=ws[i])
+                h_out[i].copy_(out, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier(world)
+        start.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        end.record(stream)
+        barrier(world)
+        e_ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
+        line["e2e"] = {"value": tokens / (e_ms / 1e3), "unit": "query-tokens/s", "ms_per_step": e_ms,
+                       "h2d_bytes_per_step": bi * world, "d2h_bytes_per_step": bo * world,
+                       "api": "dsa_attention.dsa_forward (C ABI dsa_forward), pinned host buffers"}
+        line["gpu_launches"] += 3 * len(blocks) * args.steps
+        del h_key, h_rows, d_key, d_rows, ws, h_out
+
+    # ---- CPU baseline (rank 0 at N=1 only)
+    if world == 1 and rank == 0 and not args.no_cpu:
+        ctx = cpu_reference_setup(cfg, inputs)
+        rate, rows, el = cpu_reference_rate(ctx, cfg, args.cpu_seconds, CHUNK[args.config])
+        line["cpu_baseline"] = {"value": rate, "unit": "query-tokens/s", "cores": ctx["threads"],
+                                "kind": cpu_kind(ctx), "sample": cpu_sample_text(ctx, cfg, rows, el)}
+    return line
+
+
+def run_reference(args, cfg, world, rank, local):
+    """The reference's own CPU implementation of the path on this host's cores."""
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    inputs = make_inputs_device(cfg, 1, dev, 0)
+    ctx = cpu_reference_setup(cfg, inputs)
+    del inputs
+    chunk = CHUNK[args.config]
+    r1, _, el1 = cpu_reference_rate(ctx, cfg, 0.0, chunk)          # probe one chunk
+    per_row = 1.0 / r1
+    step_rows = max(chunk, int(args.ref_step_seconds / per_row) // chunk * chunk)
+    step_rows = min(step_rows, cfg["T"] - cfg["T"] % chunk or chunk)
+    starts = list(range(0, cfg["T"] - step_rows + 1, chunk)) or [0]
+
+    def step(i):
+        a = starts[(i * 7919) % len(starts)]
+        for c in range(a, a + step_rows, chunk):
+            cpu_reference_rows(ctx, cfg, range(c, min(c + chunk, cfg["T"])))
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    el = time.perf_counter() - t0
+    value = step_rows * args.steps / el
+    line = base_line(args, cfg, world, value, el / args.steps * 1e3)
+    line["impl"] = "reference"
+    line["n_gpus"] = world
+    line["cpu_baseline"] = {"value": value, "unit": "query-tokens/s", "cores": ctx["threads"],
+                            "kind": cpu_kind(ctx),
+                            "sample": cpu_sample_text(ctx, cfg, step_rows * args.steps, el) +
+                            f"; {step_rows} rows per step"}
+    line["e2e"] = {"value": value, "unit": "query-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    line["gpu_launches"] = 0
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=3.0)
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        line = run_reference(args, cfg, world, rank, int(os.environ.get("LOCAL_RANK", "0")))
+        print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup()
+    line = run_b200(args, cfg, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

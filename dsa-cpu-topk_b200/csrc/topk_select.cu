@@ -192,11 +192,10 @@ template <int BLOCK>
 int launch_topk(const TopkArgs& a, cudaStream_t stream) {
     const size_t smem = (size_t)a.cache_elems * sizeof(uint32_t);
     auto kern = topk_select_kernel<BLOCK>;
-    if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-            return fail(DSA_ERR_CUDA, "topk_select: cannot set dynamic shared memory size");
-    }
+    // static + dynamic shared memory may pass 48 KB, which needs the opt-in
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return fail(DSA_ERR_CUDA, "topk_select: cannot set dynamic shared memory size");
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, BLOCK, smem) != cudaSuccess ||
         per_sm < 1)

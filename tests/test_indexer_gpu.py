@@ -29,7 +29,11 @@ def test_scores_match_golden(cuda, name):
     d = golden(name)
     out = indexer_scores_triton(t(d["q"], cuda), t(d["k"], cuda), t(d["w"], cuda), BLOCK_T=32, BLOCK_S=32)
     close(out.cpu(), t(d["scores"]), 1e-3, 1e-4)
-    agree = (topk_mask(out, 8).cpu() == t(d["mask8"])).float().mean().item()
+    # which -inf positions torch.topk picks in rows with fewer than k causal
+    # entries is unspecified, so agreement is measured on causal entries
+    T = out.shape[-1]
+    causal = torch.ones(T, T, dtype=torch.bool).tril()
+    agree = (topk_mask(out, 8).cpu() == t(d["mask8"]))[:, causal].float().mean().item()
     assert agree > 0.99
     assert (topk_mask(out, 8).sum(-1) == 8).all()
 
