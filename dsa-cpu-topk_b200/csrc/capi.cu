@@ -2,6 +2,7 @@
 // and the whole-forward pipeline (stage 1 -> 2 -> 3) over caller workspace.
 #include <math.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <string>
 
@@ -56,6 +57,13 @@ int64_t idx_cap_for(int64_t k, int64_t T_k) {
     return cap < T_k ? cap : T_k;
 }
 
+// DSA_FORCE_SIMT_INDEXER=1 routes every shape to the CUDA-core indexer
+// (used to cross-check the two kernels against each other).
+static bool force_simt() {
+    const char* e = getenv("DSA_FORCE_SIMT_INDEXER");
+    return e && e[0] == '1';
+}
+
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct ForwardLayout {
@@ -96,8 +104,10 @@ static int run_indexer(const void* q, const void* k, const float* w, float* scor
                        int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI, int dtype,
                        int fill_upper, cudaStream_t st) {
     if (indexer_tc_supported(HI, DI, dtype) && aligned16(q) && aligned16(k) && aligned16(scores) &&
-        aligned16(w))
-        return indexer_scores_tc(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, st);
+        aligned16(w) && !force_simt()) {
+        const int rc = indexer_scores_tc(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, st);
+        if (rc != -100) return rc;  // -100: shape beyond the tensor-core kernel's limits
+    }
     return indexer_scores_simt(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper, st);
 }
 

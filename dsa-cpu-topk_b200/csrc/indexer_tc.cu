@@ -1,14 +1,473 @@
 // Stage 1 (tensor-core path): tcgen05 / TMEM Lightning Indexer for bf16 inputs.
-// Not enabled yet in this build: every shape runs the fp32 CUDA-core kernel.
+//
+//   I[b,t,s] = sum_j w[b,t,j] * ReLU(<q[b,t,j,:], k[b,s,:]>),  s <= t
+//
+// The reference computes this with an IEEE-fp32 tl.dot per head on CUDA
+// cores (lightning_indexer.py:83-90).  Here each head's dot products are one
+// bf16 GEMM on the 5th-generation tensor cores with fp32 accumulation in
+// tensor memory, and the ReLU * w[t,j] head reduction runs in the epilogue.
+//
+// Persistent, warp-specialised, one CTA per SM:
+//   warp 0        TMA producer: per tile one key block k[s0:s0+256, :] (B operand),
+//                 then per head j the query block q[t0:t0+128, j, :] (A operand),
+//                 both 128-byte swizzled, through mbarrier rings
+//   warp 1        MMA issuer (one thread): per head, DI/16 tcgen05.mma
+//                 (M=128, N=256, K=16) into one of two TMEM accumulators
+//                 (2 x 256 columns), committed to the epilogue's barrier
+//   warps 2..9    epilogue: tcgen05.ld of the head's 128x256 fp32 tile (each
+//                 thread one query row, 128 columns), acc += w[t,j]*max(x,0)
+//                 in registers; after the last head the causal mask is applied
+//                 and the tile is stored to the fp32 score matrix
+// Tiles are the causal (query block, key block) pairs, dealt round-robin to
+// the CTAs; all warps walk the same sequence.  Every mbarrier wait is
+// bounded: on timeout the kernel records it in a device flag and leaves.
+#include <cuda.h>
+#include <math.h>
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace dsa {
 
-bool indexer_tc_supported(int64_t, int64_t, int) { return false; }
+__device__ int g_indexer_tc_timeout = 0;
 
-int indexer_scores_tc(const void*, const void*, const float*, float*, int64_t, int64_t, int64_t,
-                      int64_t, int64_t, int64_t, int, cudaStream_t) {
-    return fail(DSA_ERR_UNSUPPORTED, "indexer_scores_tc: tensor-core path not built");
+namespace {
+
+constexpr int BM = 128;            // query rows per tile (TMEM lanes)
+constexpr int BN = 256;            // keys per tile (MMA N, TMEM columns per accumulator)
+constexpr int KCH = 64;            // bf16 elements per 128-byte swizzle row
+constexpr int EPI_WARPS = 8;
+constexpr int NTHREADS = 64 + EPI_WARPS * 32;
+constexpr int MAX_TBLK = 1024;     // query blocks per batch (T_q <= 131072)
+constexpr uint32_t TMEM_COLS = 512;
+
+struct TcParams {
+    float* scores;
+    const float* w;
+    int64_t T_q, T_k, q_row0;
+    int HI, DI, B;
+    int n_tblk, nsb, tiles_per_batch, total_tiles;
+    int nA, nB;
+    uint32_t a_bytes, b_bytes;
+    int vec_store;
+};
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase of parity `parity` to complete.  Gives up after
+// ~2^24 polls (seconds), or as soon as another warp has given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(b, parity)) return true;
+        if ((i & 1023u) == 1023u) {
+            if (*(volatile int*)&g_indexer_tc_timeout) return false;
+            if (i >= (1u << 24)) {
+                atomicExch(&g_indexer_tc_timeout, 1);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,
+// 8-row core groups 1024 bytes apart (SBO), sm_100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;             // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;   // SBO
+    d |= (uint64_t)1 << 46;             // version
+    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+    return d;
+}
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// tile index -> (batch, query block, key block) through the per-batch prefix
+// of key blocks per query block
+__device__ __forceinline__ void decode_tile(int lin, const int* pref, const TcParams& p, int& b,
+                                            int& i, int& j) {
+    b = lin / p.tiles_per_batch;
+    const int r = lin - b * p.tiles_per_batch;
+    int lo = 0, hi = p.n_tblk - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pref[mid] <= r) lo = mid;
+        else hi = mid - 1;
+    }
+    i = lo;
+    j = r - pref[lo];
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    indexer_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                      const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int pref[MAX_TBLK + 1];
+    __shared__ uint32_t tmem_slot;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + (size_t)p.nA * p.a_bytes;
+    uint64_t* fullA = reinterpret_cast<uint64_t*>(sB + (size_t)p.nB * p.b_bytes);
+    uint64_t* emptyA = fullA + p.nA;
+    uint64_t* fullB = emptyA + p.nA;
+    uint64_t* emptyB = fullB + p.nB;
+    uint64_t* tfull = emptyB + p.nB;
+    uint64_t* tempty = tfull + 2;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = p.DI / KCH;
+
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int i = 0; i < p.n_tblk; ++i) {
+            pref[i] = acc;
+            int64_t tq_end = (int64_t)(i + 1) * BM;
+            if (tq_end > p.T_q) tq_end = p.T_q;
+            const int64_t t_max = p.q_row0 + tq_end - 1;
+            int64_t c = t_max / BN + 1;
+            if (c > p.nsb) c = p.nsb;
+            acc += (int)c;
+        }
+        pref[p.n_tblk] = acc;
+    }
+    if (threadIdx.x == 32) {
+        for (int s = 0; s < p.nA; ++s) {
+            mbar_init(&fullA[s], 1);
+            mbar_init(&emptyA[s], 1);
+        }
+        for (int s = 0; s < p.nB; ++s) {
+            mbar_init(&fullB[s], 1);
+            mbar_init(&emptyB[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&tfull[s], 1);
+            mbar_init(&tempty[s], EPI_WARPS);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int as = 0, bs = 0;
+            uint32_t aph = 0, bph = 0;
+            bool ok = true;
+            for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
+                int b, i, j;
+                decode_tile(lin, pref, p, b, i, j);
+                if (!(ok = mbar_wait(&emptyB[bs], bph ^ 1))) break;
+                mbar_expect_tx(&fullB[bs], p.b_bytes);
+                for (int c = 0; c < nch; ++c)
+                    tma_load_3d(sB + (size_t)bs * p.b_bytes + (size_t)c * BN * 128, &tmk, &fullB[bs],
+                                c * KCH, j * BN, b);
+                if (++bs == p.nB) { bs = 0; bph ^= 1; }
+                for (int h = 0; h < p.HI; ++h) {
+                    if (!(ok = mbar_wait(&emptyA[as], aph ^ 1))) break;
+                    mbar_expect_tx(&fullA[as], p.a_bytes);
+                    for (int c = 0; c < nch; ++c)
+                        tma_load_4d(sA + (size_t)as * p.a_bytes + (size_t)c * BM * 128, &tmq,
+                                    &fullA[as], c * KCH, h, i * BM, b);
+                    if (++as == p.nA) { as = 0; aph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            // kind::f16: D fp32 (bit 4), A bf16 (bits 7-9), B bf16 (bits 10-12),
+            // both K-major, N>>3 at bit 17, M>>4 at bit 24
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((uint32_t)(BM >> 4) << 24);
+            int as = 0, bs = 0, tb = 0;
+            uint32_t aph = 0, bph = 0, tph = 0;
+            bool ok = true;
+            for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
+                if (!(ok = mbar_wait(&fullB[bs], bph))) break;
+                const uint32_t bbase = smem_u32(sB + (size_t)bs * p.b_bytes);
+                for (int h = 0; h < p.HI; ++h) {
+                    if (!(ok = mbar_wait(&fullA[as], aph))) break;
+                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1))) break;
+                    tc_fence_after();
+                    const uint32_t abase = smem_u32(sA + (size_t)as * p.a_bytes);
+                    const uint32_t d = tmem_base + (uint32_t)(tb * BN);
+                    for (int c = 0; c < nch; ++c) {
+#pragma unroll
+                        for (int kk = 0; kk < KCH / 16; ++kk) {
+                            const uint64_t ad = sw128_desc(abase + c * BM * 128 + kk * 32);
+                            const uint64_t bd = sw128_desc(bbase + c * BN * 128 + kk * 32);
+                            umma_bf16(d, ad, bd, idesc, (c | kk) != 0);
+                        }
+                    }
+                    umma_commit(&emptyA[as]);
+                    umma_commit(&tfull[tb]);
+                    if (++as == p.nA) { as = 0; aph ^= 1; }
+                    if (++tb == 2) { tb = 0; tph ^= 1; }
+                }
+                umma_commit(&emptyB[bs]);
+                if (++bs == p.nB) { bs = 0; bph ^= 1; }
+            }
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int ew = warp - 2;
+        const int quarter = warp & 3;       // TMEM lanes this warp may read
+        const int half = ew >> 2;           // which 128 of the 256 columns
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        int tb = 0;
+        uint32_t tph = 0;
+        bool ok = true;
+        for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
+            int b, i, j;
+            decode_tile(lin, pref, p, b, i, j);
+            const int64_t tq = (int64_t)i * BM + row;
+            const bool row_ok = tq < p.T_q;
+            const float* wrow = p.w + ((int64_t)b * p.T_q + (row_ok ? tq : 0)) * p.HI;
+            float acc[128];
+#pragma unroll
+            for (int c = 0; c < 128; ++c) acc[c] = 0.f;
+            float wn = row_ok ? __ldg(wrow) : 0.f;
+            for (int h = 0; h < p.HI; ++h) {
+                const float wj = wn;
+                if (h + 1 < p.HI) wn = row_ok ? __ldg(wrow + h + 1) : 0.f;
+                if (!(ok = mbar_wait(&tfull[tb], tph))) break;
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + half * 128);
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    uint32_t r[32];
+                    tmem_ld32(taddr + ch * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        acc[ch * 32 + e] = fmaf(wj, fmaxf(__uint_as_float(r[e]), 0.f), acc[ch * 32 + e]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[tb]);
+                if (++tb == 2) { tb = 0; tph ^= 1; }
+            }
+            if (!ok || !row_ok) continue;
+            const int64_t t = p.q_row0 + tq;
+            const int64_t s0 = (int64_t)j * BN + half * 128;
+            float* out = p.scores + ((int64_t)b * p.T_q + tq) * p.T_k + s0;
+            const float NEG = -INFINITY;
+            if (p.vec_store && s0 + 128 <= p.T_k) {
+#pragma unroll
+                for (int c = 0; c < 128; c += 4) {
+                    float4 v;
+                    v.x = (s0 + c + 0 <= t) ? acc[c + 0] : NEG;
+                    v.y = (s0 + c + 1 <= t) ? acc[c + 1] : NEG;
+                    v.z = (s0 + c + 2 <= t) ? acc[c + 2] : NEG;
+                    v.w = (s0 + c + 3 <= t) ? acc[c + 3] : NEG;
+                    *reinterpret_cast<float4*>(out + c) = v;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 128; ++c)
+                    if (s0 + c < p.T_k) out[c] = (s0 + c <= t) ? acc[c] : NEG;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// -inf for every s > t (the full-matrix contract of the score output)
+__global__ void fill_upper_kernel(float* scores, int64_t T_q, int64_t T_k, int64_t q_row0) {
+    const int64_t row = blockIdx.x;  // b * T_q + tq
+    const int64_t t = q_row0 + row % T_q;
+    float* out = scores + row * T_k;
+    for (int64_t s = t + 1 + threadIdx.x; s < T_k; s += blockDim.x) out[s] = -INFINITY;
+}
+
+}  // namespace
+
+bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype) {
+    return dtype == DSA_BF16 && (DI == 64 || DI == 128) && HI >= 1 && HI <= 4096;
+}
+
+static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                      const cuuint64_t* strides, const cuuint32_t* box, const char* what) {
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = cuTensorMapEncodeTiled(
+        m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
+        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(DSA_ERR_CUDA, std::string("indexer_tc: cuTensorMapEncodeTiled failed for ") + what +
+                                      " (" + std::to_string((int)r) + ")");
+    return DSA_OK;
+}
+
+int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
+                      int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
+                      int fill_upper, cudaStream_t stream) {
+    TcParams p;
+    p.scores = scores;
+    p.w = w;
+    p.T_q = T_q;
+    p.T_k = T_k;
+    p.q_row0 = q_row0;
+    p.HI = (int)HI;
+    p.DI = (int)DI;
+    p.B = (int)B;
+    p.n_tblk = (int)((T_q + BM - 1) / BM);
+    p.nsb = (int)((T_k + BN - 1) / BN);
+    if (p.n_tblk > MAX_TBLK) return -100;  // caller falls back to the CUDA-core kernel
+    int64_t per_batch = 0;
+    for (int i = 0; i < p.n_tblk; ++i) {
+        int64_t tq_end = (int64_t)(i + 1) * BM;
+        if (tq_end > T_q) tq_end = T_q;
+        int64_t c = (q_row0 + tq_end - 1) / BN + 1;
+        if (c > p.nsb) c = p.nsb;
+        per_batch += c;
+    }
+    if (per_batch * B > INT32_MAX) return -100;
+    p.tiles_per_batch = (int)per_batch;
+    p.total_tiles = (int)(per_batch * B);
+    p.a_bytes = (uint32_t)(BM * DI * 2);
+    p.b_bytes = (uint32_t)(BN * DI * 2);
+    p.vec_store = (T_k % 4 == 0) ? 1 : 0;
+
+    // shared memory: the device's opt-in limit minus the kernel's static
+    // shared memory; 1 KB alignment slack + rings + barriers
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, indexer_tc_kernel) != cudaSuccess)
+        return fail(DSA_ERR_CUDA, "indexer_tc: cannot query shared memory limits");
+    const size_t kMaxSmem = (size_t)optin - fa.sharedSizeBytes;
+    const size_t fixed = 1024 + 256;
+    const char* env_nb = getenv("DSA_TC_NB");  // ring depth of the key operand (1 or 2)
+    p.nB = (env_nb && env_nb[0] == '1') ? 1 : 2;
+    if (kMaxSmem < fixed + (size_t)p.nB * p.b_bytes + 2 * (size_t)p.a_bytes) p.nB = 1;
+    p.nA = (int)((kMaxSmem - fixed - (size_t)p.nB * p.b_bytes) / p.a_bytes);
+    if (p.nA > 8) p.nA = 8;
+    if (p.nA < 2) return -100;
+    const size_t smem = fixed + (size_t)p.nA * p.a_bytes + (size_t)p.nB * p.b_bytes;
+
+    if (fill_upper) {
+        fill_upper_kernel<<<(unsigned)(B * T_q), 256, 0, stream>>>(scores, T_q, T_k, q_row0);
+        int rc = check_launch("fill_upper_kernel");
+        if (rc) return rc;
+    }
+    if (p.total_tiles == 0) return DSA_OK;
+
+    CUtensorMap tmq, tmk;
+    {
+        const cuuint64_t dims[4] = {(cuuint64_t)DI, (cuuint64_t)HI, (cuuint64_t)T_q, (cuuint64_t)B};
+        const cuuint64_t str[3] = {(cuuint64_t)DI * 2, (cuuint64_t)HI * DI * 2,
+                                   (cuuint64_t)T_q * HI * DI * 2};
+        const cuuint32_t box[4] = {KCH, 1, BM, 1};
+        int rc = encode_map(&tmq, q, 4, dims, str, box, "q");
+        if (rc) return rc;
+    }
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)DI, (cuuint64_t)T_k, (cuuint64_t)B};
+        const cuuint64_t str[2] = {(cuuint64_t)DI * 2, (cuuint64_t)T_k * DI * 2};
+        const cuuint32_t box[3] = {KCH, BN, 1};
+        int rc = encode_map(&tmk, k, 3, dims, str, box, "k");
+        if (rc) return rc;
+    }
+    if (cudaFuncSetAttribute(indexer_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return fail(DSA_ERR_CUDA, "indexer_tc: cannot set dynamic shared memory size");
+    int grid = num_sms();
+    if (grid > p.total_tiles) grid = p.total_tiles;
+    indexer_tc_kernel<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, p);
+    return check_launch("indexer_tc_kernel");
 }
 
 }  // namespace dsa

@@ -1,0 +1,74 @@
+"""GPU: the tcgen05 tensor-core indexer (bf16, DI in {64, 128}) against the
+fp32 CUDA-core kernel and the oracle, on ragged shapes.
+
+Both GPU kernels compute from identical bf16 inputs; they differ only in
+fp32 summation order, so they agree to ~1e-5 relative; the oracle (fp32
+einsum of the upcast inputs) to rtol 2e-2 (the bf16 parity bar), in practice
+far tighter."""
+import os
+
+import pytest
+import torch
+
+import dsa_oracle as o
+
+pytestmark = pytest.mark.gpu
+
+
+def scores(q, k, w, **kw):
+    from lightning_indexer import indexer_scores
+    return indexer_scores(q, k, w, **kw)
+
+
+def simt_scores(q, k, w, **kw):
+    os.environ["DSA_FORCE_SIMT_INDEXER"] = "1"
+    try:
+        return scores(q, k, w, **kw)
+    finally:
+        del os.environ["DSA_FORCE_SIMT_INDEXER"]
+
+
+@pytest.mark.parametrize("B,T_q,T_k,q0,HI,DI", [
+    (1, 256, 256, 0, 4, 64),
+    (1, 300, 300, 0, 3, 128),       # ragged query and key blocks
+    (2, 1000, 1000, 0, 16, 64),
+    (1, 129, 1001, 872, 8, 128),    # row block at an offset, T_k % 4 != 0
+    (3, 1, 513, 512, 2, 64),        # single query row
+    (1, 2048, 2048, 0, 64, 128),    # c5 head shapes
+])
+def test_tc_matches_simt_and_oracle(cuda, B, T_q, T_k, q0, HI, DI):
+    g = torch.Generator().manual_seed(T_q + 7 * HI)
+    q = torch.randn(B, T_q, HI, DI, generator=g).bfloat16()
+    k = torch.randn(B, T_k, DI, generator=g).bfloat16()
+    w = torch.randn(B, T_q, HI, generator=g) / HI ** 0.5
+    dq, dk, dw = q.to(cuda), k.to(cuda), w.to(cuda)
+    tc = scores(dq, dk, dw, q_row0=q0).cpu()
+    sm = simt_scores(dq, dk, dw, q_row0=q0).cpu()
+    fin = torch.isfinite(sm)
+    assert torch.equal(torch.isfinite(tc), fin)
+    assert torch.isneginf(tc[~fin]).all()
+    err = (tc[fin] - sm[fin]).abs()
+    scale = torch.einsum("bthd,bsd->bts", q.float().abs(), k.float().abs()).mean().item()
+    assert err.max().item() < 1e-5 * scale * HI ** 0.5 + 1e-6, err.max().item()
+    # oracle on the absolute rows
+    qf = torch.zeros(B, q0 + T_q, HI, DI)
+    wf = torch.zeros(B, q0 + T_q, HI)
+    qf[:, q0:], wf[:, q0:] = q.float(), w
+    kf = k.float()
+    if kf.shape[1] < qf.shape[1]:
+        kf = torch.cat([kf, torch.zeros(B, qf.shape[1] - kf.shape[1], DI)], 1)
+    ref = o.indexer_scores(qf, kf, wf, slice(q0, q0 + T_q), T_k=T_k)
+    assert torch.equal(torch.isfinite(ref), fin)
+    e2 = (tc[fin] - ref[fin]).abs()
+    assert bool((e2 <= 2e-2 * ref[fin].abs() + 1e-4 * scale).all()), e2.max().item()
+
+
+def test_tc_fill_upper_contract(cuda):
+    q = torch.randn(1, 384, 4, 64).bfloat16().to(cuda)
+    k = torch.randn(1, 384, 64).bfloat16().to(cuda)
+    w = torch.randn(1, 384, 4).to(cuda)
+    full = scores(q, k, w, fill_upper=True)
+    upper = ~torch.ones(384, 384, dtype=torch.bool, device=cuda).tril()
+    assert torch.isneginf(full[0][upper]).all()
+    part = scores(q, k, w, fill_upper=False)
+    assert torch.equal(part[0][~upper], full[0][~upper])
