@@ -377,10 +377,32 @@ bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype) {
     return dtype == DSA_BF16 && (DI == 64 || DI == 128) && HI >= 1 && HI <= 4096;
 }
 
+// cuTensorMapEncodeTiled is looked up through the runtime, so the library
+// does not link libcuda (it loads on hosts without a driver).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
 static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
                       const cuuint64_t* strides, const cuuint32_t* box, const char* what) {
     const cuuint32_t estr[4] = {1, 1, 1, 1};
-    const CUresult r = cuTensorMapEncodeTiled(
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(DSA_ERR_CUDA, "indexer_tc: cuTensorMapEncodeTiled not available");
+    const CUresult r = enc(
         m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
