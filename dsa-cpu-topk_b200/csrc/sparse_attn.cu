@@ -5,19 +5,22 @@
 // masks, with a kernel that touches only the kept rows: O(k) bytes per query
 // instead of O(T).
 //
-// One CTA per query row.  A "team" of L = HQ * D / VEC threads covers one
-// key row (all heads) with one 16-byte load per thread, so every gathered K
-// or V row is read as fully coalesced 16-byte vectors; G = D / VEC lanes of a
-// team hold one head and reduce its dot product with xor-shuffles.  The CTA
-// holds BLOCK / L teams which walk the key list with a stride, each keeping
+// One CTA per query row.  A "team" of L threads covers one key row (all
+// heads): each thread owns up to two 16-byte chunks of one head (interleaved with
+// the head's other lanes, so every load instruction is contiguous per head),
+// and the G lanes that share a head reduce its dot product with log2(G)
+// xor-shuffles.  Products and the p*V accumulation use packed fp32x2 FMAs.
+// The CTA's BLOCK / L teams walk the key list with a stride, each keeping
 // its own running max / sum / accumulator (online softmax over blocks of U
-// keys, exp2 domain), merged through shared memory at the end.
+// keys in the exp2 domain, rescaled only when the max grows by more than
+// 2^8), and merge through shared memory at the end.
 //
 // The key list comes either from dsa_topk_select's index list (list form) or
 // from scanning the score row against the threshold (threshold form, and the
 // fallback for a row whose kept count overflowed the list capacity).  Both
 // visit kept keys in ascending position order.
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -41,46 +44,105 @@ struct AttnArgs {
 };
 
 constexpr float kNegInf = -INFINITY;
+// Rescale the running output only when a new logit exceeds the running max by
+// more than this many log2 units; until then exp2(x - m) <= 2^8 stays exact
+// enough in fp32 and the final division by l cancels the stale max.
+constexpr float kRescale = 8.f;
 
-template <typename T, int G, int BLOCK, int U>
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)),
+          "l"(*reinterpret_cast<unsigned long long*>(&b)),
+          "l"(*reinterpret_cast<unsigned long long*>(&c)));
+    return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)),
+          "l"(*reinterpret_cast<unsigned long long*>(&b)));
+    return *reinterpret_cast<float2*>(&d);
+}
+
+// one 32-bit word of T data -> the float pair it holds
+template <typename T> __device__ __forceinline__ float2 word2(uint32_t w);
+template <> __device__ __forceinline__ float2 word2<__nv_bfloat16>(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 word2<__half>(uint32_t w) {
+    return __half22float2(*reinterpret_cast<__half2*>(&w));
+}
+// fp32 data: two words make one pair
+template <typename T> struct Pairs {  // 16-bit types: 4 words -> 4 pairs per 16 bytes
+    static constexpr int PER16 = 4;
+    static __device__ __forceinline__ float2 get(const uint4& v, int i) {
+        const uint32_t w = i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+        return word2<T>(w);
+    }
+};
+template <> struct Pairs<float> {
+    static constexpr int PER16 = 2;
+    static __device__ __forceinline__ float2 get(const uint4& v, int i) {
+        return i == 0 ? make_float2(__uint_as_float(v.x), __uint_as_float(v.y))
+                      : make_float2(__uint_as_float(v.z), __uint_as_float(v.w));
+    }
+};
+
+// One CTA per query row.  A team of L = HQ*G threads covers a key row; each
+// thread owns C contiguous 16-byte chunks (E elements) of one head, so the
+// G lanes of a head reduce with log2(G) shuffles.  The P = BLOCK/L teams
+// stride over the key list and merge at the end.
+template <typename T, int C, int G, int BLOCK, int U>
 __global__ void __launch_bounds__(BLOCK) sparse_attn_kernel(AttnArgs<T> a) {
     constexpr int VEC = 16 / sizeof(T);
+    constexpr int E = C * VEC;          // elements per thread
+    constexpr int NP = E / 2;           // float pairs per thread
+    constexpr int PP = Pairs<T>::PER16; // pairs per 16-byte chunk
     constexpr int NW = BLOCK / 32;
-    constexpr int LIST = BLOCK;  // keys staged per refill
+    constexpr int LIST = BLOCK;
     __shared__ int32_t keys_s[LIST];
     __shared__ uint32_t warp_tot[NW];
     __shared__ int s_n;
-    __shared__ float m_s[BLOCK], l_s[BLOCK];        // per (team, head) — at most BLOCK entries
-    __shared__ float acc_s[BLOCK * VEC];             // per (team, lane) partial outputs
+    extern __shared__ float merge_s[];  // [P*HQ] m, [P*HQ] l, [P*L*E] acc
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int L = a.HQ * G;          // threads per key row
-    const int P = BLOCK / L;         // teams
+    const int L = a.HQ * G;
+    const int P = BLOCK / L;
     const int team = tid / L;
-    const int lt = tid - team * L;   // lane within team: head h = lt / G
-    const bool active = team < P;    // threads beyond P*L idle in the math
+    const int lt = tid - team * L;
+    const bool active = team < P;
 
     const int64_t row = blockIdx.x;
     const int64_t b = row / a.T_q;
     const int64_t t = a.q_row0 + (row - b * a.T_q);
     const int64_t valid = t + 1 < a.T_k ? t + 1 : a.T_k;
-    const int64_t rowlen = (int64_t)a.HQ * a.D;  // elements per K/V row
-    const T* Kb = a.K + b * a.T_k * rowlen + (int64_t)lt * VEC;
-    const T* Vb = a.V + b * a.T_k * rowlen + (int64_t)lt * VEC;
+    const int64_t rowlen = (int64_t)a.HQ * a.D;
+    // lane g of head h owns chunks g, g+G, ..., g+(C-1)G of the head, so each
+    // chunk-load instruction reads a contiguous span per head
+    const int64_t toff = (int64_t)(lt / G) * a.D + (lt % G) * VEC;
+    const T* Kb = a.K + b * a.T_k * rowlen + toff;
+    const T* Vb = a.V + b * a.T_k * rowlen + toff;
 
-    float q[VEC], acc[VEC];
+    float2 q[NP], acc[NP];
     {
-        const uint4 qv = active ? ldg16(a.Q + row * rowlen + (int64_t)lt * VEC) : make_uint4(0, 0, 0, 0);
-        unpack16<T>(qv, q);
+        const T* qp = a.Q + row * rowlen + toff;
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-            q[v] *= a.scale_log2;
-            acc[v] = 0.f;
+        for (int c = 0; c < C; ++c) {
+            const uint4 v = active ? ldg16(qp + c * G * VEC) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int i = 0; i < PP; ++i) {
+                const float2 f = Pairs<T>::get(v, i);
+                q[c * PP + i] = make_float2(f.x * a.scale_log2, f.y * a.scale_log2);
+            }
         }
+#pragma unroll
+        for (int i = 0; i < NP; ++i) acc[i] = make_float2(0.f, 0.f);
     }
     float m = kNegInf, l = 0.f;
 
-    // list form unless the row's kept count overflowed the list
     int64_t n_total;
     bool list_mode = false;
     if (a.idx) {
@@ -101,7 +163,6 @@ __global__ void __launch_bounds__(BLOCK) sparse_attn_kernel(AttnArgs<T> a) {
             for (int i = tid; i < n; i += BLOCK) keys_s[i] = __ldg(a.idx + row * a.idx_cap + c0 + i);
             __syncthreads();
         } else {
-            // ordered compaction of positions c0 + tid with score >= thr
             const int64_t s = c0 + tid;
             const bool p = s < n_total && __ldg(srow + s) >= thr;
             const uint32_t bal = __ballot_sync(0xffffffffu, p);
@@ -119,114 +180,140 @@ __global__ void __launch_bounds__(BLOCK) sparse_attn_kernel(AttnArgs<T> a) {
             n = s_n;
         }
 
-        // every thread runs the same trip count so shuffles stay warp-uniform
         for (int base = 0; base < n; base += P * U) {
-            uint4 kr[U], vr[U];
+            uint4 kr[U][C], vr[U][C];
             bool ok[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int j = base + team + u * P;
                 ok[u] = active && j < n;
-                const int64_t s = ok[u] ? keys_s[j] : 0;
-                if (ok[u]) {
-                    kr[u] = ldg16(Kb + s * rowlen);
-                    vr[u] = ldg16(Vb + s * rowlen);
-                } else {
-                    kr[u] = make_uint4(0, 0, 0, 0);
-                    vr[u] = make_uint4(0, 0, 0, 0);
+                const int64_t off = (ok[u] ? (int64_t)keys_s[j] : 0) * rowlen;
+#pragma unroll
+                for (int c = 0; c < C; ++c) {
+                    kr[u][c] = ok[u] ? ldg16(Kb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                    vr[u][c] = ok[u] ? ldg16(Vb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
                 }
             }
             float x[U];
-            float mx = m;
+            float mx = kNegInf;
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                float kf[VEC];
-                unpack16<T>(kr[u], kf);
-                float d = 0.f;
+                float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int v = 0; v < VEC; ++v) d = fmaf(q[v], kf[v], d);
+                for (int c = 0; c < C; ++c)
+#pragma unroll
+                    for (int i = 0; i < PP; ++i) d2 = ffma2(q[c * PP + i], Pairs<T>::get(kr[u][c], i), d2);
+                float d = d2.x + d2.y;
 #pragma unroll
                 for (int o = G / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
                 x[u] = ok[u] ? d : kNegInf;
                 mx = fmaxf(mx, x[u]);
             }
-            if (mx != kNegInf) {
+            if (mx > m + kRescale) {  // also true on the first key (m = -inf)
                 const float corr = exp2f(m - mx);
+                const float2 c2 = make_float2(corr, corr);
                 l *= corr;
 #pragma unroll
-                for (int v = 0; v < VEC; ++v) acc[v] *= corr;
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const float p = exp2f(x[u] - mx);  // 0 for skipped slots
-                    l += p;
-                    float vf[VEC];
-                    unpack16<T>(vr[u], vf);
-#pragma unroll
-                    for (int v = 0; v < VEC; ++v) acc[v] = fmaf(p, vf[v], acc[v]);
-                }
+                for (int i = 0; i < NP; ++i) acc[i] = fmul2(acc[i], c2);
                 m = mx;
             }
+            if (m == kNegInf) continue;  // no key of this team in the block yet
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float p = exp2f(x[u] - m);  // 0 for skipped slots
+                l += p;
+                const float2 p2 = make_float2(p, p);
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+#pragma unroll
+                    for (int i = 0; i < PP; ++i)
+                        acc[c * PP + i] = ffma2(p2, Pairs<T>::get(vr[u][c], i), acc[c * PP + i]);
+            }
         }
-        __syncthreads();  // keys_s is refilled by the next chunk
+        __syncthreads();
     }
 
-    // merge the teams and write O[row] (fp32, [HQ, DV])
-    float* orow = a.O + row * rowlen + (int64_t)lt * VEC;
+    float* orow = a.O + row * rowlen + toff;
     if (P == 1) {
         if (active) {
             const float inv = 1.f / l;
 #pragma unroll
-            for (int v = 0; v < VEC; v += 4)
-                *reinterpret_cast<float4*>(orow + v) =
-                    make_float4(acc[v] * inv, acc[v + 1] * inv, acc[v + 2] * inv, acc[v + 3] * inv);
+            for (int c = 0; c < C; ++c)
+#pragma unroll
+                for (int i = 0; i < PP; i += 2) {
+                    const float2 x0 = acc[c * PP + i], x1 = acc[c * PP + i + 1];
+                    *reinterpret_cast<float4*>(orow + c * G * VEC + 2 * i) =
+                        make_float4(x0.x * inv, x0.y * inv, x1.x * inv, x1.y * inv);
+                }
         }
         return;
     }
+    float* m_s = merge_s;
+    float* l_s = m_s + P * a.HQ;
+    float* acc_s = l_s + P * a.HQ;
     if (active) {
         if (lt % G == 0) {
             m_s[team * a.HQ + lt / G] = m;
             l_s[team * a.HQ + lt / G] = l;
         }
+        // partial outputs in row layout: acc_s[team][element of the row]
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) acc_s[(team * L + lt) * VEC + v] = acc[v];
+        for (int c = 0; c < C; ++c)
+#pragma unroll
+            for (int i = 0; i < PP; ++i)
+                *reinterpret_cast<float2*>(&acc_s[team * rowlen + toff + c * G * VEC + 2 * i]) =
+                    acc[c * PP + i];
     }
     __syncthreads();
-    if (team == 0) {
-        const int h = lt / G;
+    // all threads share the output: element e of the row (e = lt*E + ...)
+    for (int e = tid; e < L * E; e += BLOCK) {
+        const int h = e / a.D;
         float mstar = kNegInf;
         for (int p = 0; p < P; ++p) mstar = fmaxf(mstar, m_s[p * a.HQ + h]);
-        float lsum = 0.f, o[VEC];
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) o[v] = 0.f;
+        float lsum = 0.f, o = 0.f;
         for (int p = 0; p < P; ++p) {
             const float mp = m_s[p * a.HQ + h];
             const float f = mp == kNegInf ? 0.f : exp2f(mp - mstar);
             lsum += l_s[p * a.HQ + h] * f;
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) o[v] = fmaf(acc_s[(p * L + lt) * VEC + v], f, o[v]);
+            o = fmaf(acc_s[p * rowlen + e], f, o);
         }
-        const float inv = 1.f / lsum;
-#pragma unroll
-        for (int v = 0; v < VEC; v += 4)
-            *reinterpret_cast<float4*>(orow + v) =
-                make_float4(o[v] * inv, o[v + 1] * inv, o[v + 2] * inv, o[v + 3] * inv);
+        a.O[row * rowlen + e] = o / lsum;
     }
 }
 
-template <typename T, int G>
+template <typename T, int C, int G>
 int launch_g(const AttnArgs<T>& a, cudaStream_t stream) {
+    constexpr int VEC = 16 / sizeof(T);
+    constexpr int E = C * VEC;
     const int L = a.HQ * G;
     const int64_t rows = a.B * a.T_q;
     if (rows > INT32_MAX) return fail(DSA_ERR_INVALID, "sparse_attn: too many query rows");
-    if (L <= 256) {
-        sparse_attn_kernel<T, G, 256, 4><<<(unsigned)rows, 256, 0, stream>>>(a);
-    } else if (L <= 512) {
-        sparse_attn_kernel<T, G, 512, 4><<<(unsigned)rows, 512, 0, stream>>>(a);
-    } else if (L <= 1024) {
-        sparse_attn_kernel<T, G, 1024, 2><<<(unsigned)rows, 1024, 0, stream>>>(a);
-    } else {
-        return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: HQ*D too large for one CTA per key row");
+    int block;
+    if (L <= 256) block = 256;
+    else if (L <= 512) block = 512;
+    else if (L <= 1024) block = 1024;
+    else return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: HQ*D too large for one CTA per key row");
+    const int P = block / L;
+    const size_t smem = P == 1 ? 0 : (size_t)(2 * P * a.HQ + P * L * E) * sizeof(float);
+#define DSA_LAUNCH(BLK, UU)                                                                           \
+    {                                                                                                 \
+        auto kern = sparse_attn_kernel<T, C, G, BLK, UU>;                                             \
+        if (smem > 48 * 1024 &&                                                                       \
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=     \
+                cudaSuccess)                                                                          \
+            return fail(DSA_ERR_CUDA, "sparse_attn: cannot set dynamic shared memory size");        \
+        kern<<<(unsigned)rows, BLK, smem, stream>>>(a);                                               \
     }
+    static const int u_env = [] {
+        const char* e = getenv("DSA_ATTN_U");  // keys per team per step (2 or 4)
+        return (e && e[0] == '4') ? 4 : 2;
+    }();
+    if (block == 256) {
+        if (u_env == 4) DSA_LAUNCH(256, 4)
+        else DSA_LAUNCH(256, 2)
+    } else if (block == 512) DSA_LAUNCH(512, 2)
+    else DSA_LAUNCH(1024, 1)
+#undef DSA_LAUNCH
     return check_launch("sparse_attn_kernel");
 }
 
@@ -236,17 +323,18 @@ int launch_t(AttnArgs<T> a, cudaStream_t stream) {
     if (a.D % VEC != 0)
         return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: head dim must be a multiple of " +
                                              std::to_string(VEC) + " for this dtype");
-    const int G = a.D / VEC;
-    switch (G) {
-        case 1: return launch_g<T, 1>(a, stream);
-        case 2: return launch_g<T, 2>(a, stream);
-        case 4: return launch_g<T, 4>(a, stream);
-        case 8: return launch_g<T, 8>(a, stream);
-        case 16: return launch_g<T, 16>(a, stream);
-        case 32: return launch_g<T, 32>(a, stream);
+    const int chunks = a.D / VEC;  // 16-byte chunks per head
+    switch (chunks) {
+        case 1: return launch_g<T, 1, 1>(a, stream);
+        case 2: return launch_g<T, 2, 1>(a, stream);
+        case 4: return launch_g<T, 2, 2>(a, stream);
+        case 8: return launch_g<T, 2, 4>(a, stream);
+        case 16: return launch_g<T, 2, 8>(a, stream);
+        case 32: return launch_g<T, 2, 16>(a, stream);
+        case 64: return launch_g<T, 2, 32>(a, stream);
         default:
             return fail(DSA_ERR_UNSUPPORTED,
-                        "sparse_attn: head dim / (16 bytes / element) must be a power of two <= 32");
+                        "sparse_attn: head dim / (16 bytes / element) must be a power of two <= 64");
     }
 }
 

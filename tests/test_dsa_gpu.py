@@ -75,6 +75,8 @@ def test_list_form_overflow_rows_fall_back(cuda):
     (4, 512, 4, 32, 4, 32, 128, torch.float32),    # config c3 corner
     (1, 1000, 8, 64, 8, 64, 100, torch.bfloat16),  # ragged bf16
     (1, 2048, 16, 64, 16, 64, 512, torch.bfloat16),  # c4 head shapes, shorter T
+    (1, 1500, 8, 128, 16, 128, 256, torch.bfloat16),  # c5 head shapes (tensor-core indexer)
+    (2, 600, 4, 64, 3, 16, 40, torch.float16),     # fp16, tiny heads
     (3, 77, 2, 16, 2, 16, 80, torch.float32),      # k > T: every causal key kept
     (1, 300, 4, 32, 2, 128, 16, torch.float32),    # D = 128 fp32
     (1, 300, 4, 32, 8, 256, 16, torch.bfloat16),   # D = 256 bf16 (1024-thread rows)
