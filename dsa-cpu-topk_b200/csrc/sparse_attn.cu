@@ -95,8 +95,8 @@ template <> struct Pairs<float> {
 // thread owns C contiguous 16-byte chunks (E elements) of one head, so the
 // G lanes of a head reduce with log2(G) shuffles.  The P = BLOCK/L teams
 // stride over the key list and merge at the end.
-template <typename T, int C, int G, int BLOCK, int U>
-__global__ void __launch_bounds__(BLOCK) sparse_attn_kernel(AttnArgs<T> a) {
+template <typename T, int C, int G, int BLOCK, int U, int MINB>
+__global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a) {
     constexpr int VEC = 16 / sizeof(T);
     constexpr int E = C * VEC;          // elements per thread
     constexpr int NP = E / 2;           // float pairs per thread
@@ -295,24 +295,20 @@ int launch_g(const AttnArgs<T>& a, cudaStream_t stream) {
     else return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: HQ*D too large for one CTA per key row");
     const int P = block / L;
     const size_t smem = P == 1 ? 0 : (size_t)(2 * P * a.HQ + P * L * E) * sizeof(float);
-#define DSA_LAUNCH(BLK, UU)                                                                           \
+#define DSA_LAUNCH(BLK, UU, MB)                                                                   \
     {                                                                                                 \
-        auto kern = sparse_attn_kernel<T, C, G, BLK, UU>;                                             \
+        auto kern = sparse_attn_kernel<T, C, G, BLK, UU, MB>;                                     \
         if (smem > 48 * 1024 &&                                                                       \
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=     \
                 cudaSuccess)                                                                          \
             return fail(DSA_ERR_CUDA, "sparse_attn: cannot set dynamic shared memory size");        \
         kern<<<(unsigned)rows, BLK, smem, stream>>>(a);                                               \
     }
-    static const int u_env = [] {
-        const char* e = getenv("DSA_ATTN_U");  // keys per team per step (2 or 4)
-        return (e && e[0] == '4') ? 4 : 2;
-    }();
-    if (block == 256) {
-        if (u_env == 4) DSA_LAUNCH(256, 4)
-        else DSA_LAUNCH(256, 2)
-    } else if (block == 512) DSA_LAUNCH(512, 2)
-    else DSA_LAUNCH(1024, 1)
+    // 256 threads: two keys in flight per team, 4 CTAs per SM (80 -> 64
+    // registers) measured best on B200 among U in {1, 2, 4} and 3 or 4 CTAs/SM
+    if (block == 256) DSA_LAUNCH(256, 2, 4)
+    else if (block == 512) DSA_LAUNCH(512, 2, 1)
+    else DSA_LAUNCH(1024, 1, 1)
 #undef DSA_LAUNCH
     return check_launch("sparse_attn_kernel");
 }
