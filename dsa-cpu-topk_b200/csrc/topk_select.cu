@@ -16,6 +16,8 @@
 //
 // Selection rule (dsa_attention.py:41-46): keep every position with
 // score >= threshold (ties kept) and, for causal rows, s <= t.
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace dsa {
@@ -34,6 +36,7 @@ struct TopkArgs {
     int32_t* cnt;
     int64_t idx_cap;
     int cache_elems;
+    int cand_max;
     int vec_ok;
 };
 
@@ -206,6 +209,325 @@ int launch_topk(const TopkArgs& a, cudaStream_t stream) {
     return check_launch("topk_select_kernel");
 }
 
+// ===========================================================================
+// Rows that fit in shared memory (up to kRowCache entries, every row of the
+// reference's configurations): the fast kernel.
+//
+//   sweep 1  HBM -> key cache (float4 loads, uint4 stores) + histogram of the
+//            top 11 key bits; a block scan finds the bin d0 holding the k-th
+//            largest key
+//   sweep 2  over the cache: keys of bin d0 go with their positions to a
+//            candidate list; each warp counts the keys above bin d0 in its
+//            contiguous segment of the row
+//   passes   two radix passes (11 + 10 bits) over the candidates alone give
+//            the exact k-th largest key; kept candidates add to their
+//            segment's count
+//   sweep 3  ordered emission: a warp-wide scan of per-lane kept counts
+//            places every kept position of the warp's segment
+// A row whose bin d0 overflows the candidate buffer runs the two passes over
+// the cached row instead.  All row indexing is 32-bit.
+// ===========================================================================
+
+constexpr int kRowCache = 32768;   // keys cached per CTA (128 KB)
+constexpr int NB_TOP = 2048;       // 11-bit first digit
+
+// Exclusive block-wide prefix sum of v; *total gets the sum.  Two barriers.
+template <int BLOCK>
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* wtot, uint32_t* total) {
+    constexpr int NW = BLOCK / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) wtot[warp] = incl;
+    __syncthreads();
+    uint32_t before = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const uint32_t x = wtot[w];
+        before += w < warp ? x : 0u;
+        tot += x;
+    }
+    *total = tot;
+    __syncthreads();
+    return before + incl - v;
+}
+
+// Histograms of the fast kernel are stored in descending-digit order
+// (slot nb-1-digit), so each thread's scan range is contiguous and is read as
+// uint4s.  Finds the slot holding the krem-th largest key: res[0] = digit,
+// res[1] = rank left inside the bin.  nbins is a power of two >= 4*32.
+// Ends with a barrier.
+template <int BLOCK>
+__device__ __forceinline__ void block_find_desc(const uint32_t* hist, int nbins, uint32_t krem,
+                                                uint32_t* wtot, uint32_t* res) {
+    const int per4 = nbins >= 4 * BLOCK ? nbins / (4 * BLOCK) : 1;  // uint4s per thread
+    const bool has = (int)threadIdx.x * per4 * 4 < nbins;
+    const uint4* h4 = reinterpret_cast<const uint4*>(hist) + threadIdx.x * per4;
+    uint32_t local = 0;
+    for (int i = 0; has && i < per4; ++i) {
+        const uint4 v = h4[i];
+        local += v.x + v.y + v.z + v.w;
+    }
+    uint32_t tot;
+    const uint32_t excl = block_excl_scan<BLOCK>(local, wtot, &tot);
+    if (has && excl < krem && krem <= excl + local) {
+        uint32_t c = excl;
+        const int r0 = threadIdx.x * per4 * 4;
+        for (int i = 0; i < per4 * 4; ++i) {
+            const uint32_t h = hist[r0 + i];
+            if (krem <= c + h) {
+                res[0] = (uint32_t)(nbins - 1 - (r0 + i));
+                res[1] = krem - c;
+                break;
+            }
+            c += h;
+        }
+    }
+    __syncthreads();
+}
+
+template <int BLOCK>
+__global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
+    constexpr int NW = BLOCK / 32;
+    constexpr int S0 = 21;  // shift of the first digit
+    extern __shared__ uint4 dyn4[];
+    uint32_t* cache = reinterpret_cast<uint32_t*>(dyn4);      // cache_elems keys (multiple of 4)
+    uint32_t* cand_key = cache + a.cache_elems;               // cand_max
+    int32_t* cand_pos = reinterpret_cast<int32_t*>(cand_key + a.cand_max);
+    __shared__ __align__(16) uint32_t hist[NB_TOP];
+    __shared__ uint32_t wtot[NW];
+    __shared__ uint32_t seg_cnt[NW];
+    __shared__ uint32_t res[2];
+    __shared__ uint32_t n_cand;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
+        const float* src = a.scores + row * a.row_stride;
+        int valid = (int)a.row_len;
+        if (a.causal) {
+            const int64_t t = a.q_row0 + row % a.rows_per_batch;
+            valid = t + 1 < a.row_len ? (int)(t + 1) : (int)a.row_len;
+        }
+        if (a.k > valid) {
+            if (tid == 0) {
+                a.thr[row] = __uint_as_float(0xff800000u);
+                if (a.cnt) a.cnt[row] = valid;
+            }
+            if (a.idx) {
+                const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
+                for (int i = tid; i < n; i += BLOCK) a.idx[row * a.idx_cap + i] = i;
+            }
+            continue;
+        }
+        const int g4 = (valid + 3) >> 2;  // uint4 groups; padding keys are 0
+
+        // ---- sweep 1
+        for (int i = tid; i < NB_TOP; i += BLOCK) hist[i] = 0;
+        if (tid == 0) n_cand = 0;
+        __syncthreads();
+        if (a.vec_ok) {
+            const float4* src4 = reinterpret_cast<const float4*>(src);
+            for (int g = tid; g < g4; g += BLOCK) {
+                uint4 kk;
+                if (4 * g + 3 < valid) {
+                    const float4 v = __ldg(src4 + g);
+                    kk = make_uint4(f2key(v.x), f2key(v.y), f2key(v.z), f2key(v.w));
+                    atomicAdd(&hist[(NB_TOP - 1) - (kk.x >> S0)], 1u);
+                    atomicAdd(&hist[(NB_TOP - 1) - (kk.y >> S0)], 1u);
+                    atomicAdd(&hist[(NB_TOP - 1) - (kk.z >> S0)], 1u);
+                    atomicAdd(&hist[(NB_TOP - 1) - (kk.w >> S0)], 1u);
+                } else {
+                    uint32_t e[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
+                        if (4 * g + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
+                    }
+                    kk = make_uint4(e[0], e[1], e[2], e[3]);
+                }
+                dyn4[g] = kk;
+            }
+        } else {
+            for (int g = tid; g < g4; g += BLOCK) {
+                uint32_t e[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
+                    if (4 * g + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
+                }
+                dyn4[g] = make_uint4(e[0], e[1], e[2], e[3]);
+            }
+        }
+        __syncthreads();
+        block_find_desc<BLOCK>(hist, NB_TOP, (uint32_t)a.k, wtot, res);
+        const uint32_t d0 = res[0];
+        uint32_t krem = res[1];
+        const bool use_cand = hist[(NB_TOP - 1) - d0] <= (uint32_t)a.cand_max;
+        __syncthreads();
+
+        // warp w owns groups [w*gseg, min((w+1)*gseg, g4))
+        const int gseg = (g4 + NW - 1) / NW;
+        const int gs0 = warp * gseg;
+        const int gs1 = gs0 + gseg < g4 ? gs0 + gseg : g4;
+        uint32_t prefix = d0 << S0, pmask = ~0u << S0;
+
+        if (use_cand) {
+            // ---- sweep 2: candidates + per-segment count of keys above bin d0
+            uint32_t above = 0;
+            for (int gb = gs0; gb < gs1; gb += 32) {
+                const int g = gb + lane;
+                uint4 kk = g < gs1 ? dyn4[g] : make_uint4(0, 0, 0, 0);
+                const uint32_t e[4] = {kk.x, kk.y, kk.z, kk.w};
+                uint32_t nin = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    above += (e[j] >> S0) > d0;
+                    nin += (e[j] >> S0) == d0;
+                }
+                // padding keys are 0: digit 0, never == d0 for finite data
+                if (__any_sync(0xffffffffu, nin != 0)) {
+                    uint32_t pre = nin;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t y = __shfl_up_sync(0xffffffffu, pre, o);
+                        if (lane >= o) pre += y;
+                    }
+                    uint32_t base = 0;
+                    if (lane == 31) base = atomicAdd(&n_cand, pre);
+                    base = __shfl_sync(0xffffffffu, base, 31) + pre - nin;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if ((e[j] >> S0) == d0) {
+                            cand_key[base] = e[j];
+                            cand_pos[base] = 4 * g + j;
+                            ++base;
+                        }
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) above += __shfl_xor_sync(0xffffffffu, above, o);
+            if (lane == 0) seg_cnt[warp] = above;
+            __syncthreads();
+            const int nc = (int)n_cand;
+#pragma unroll 1
+            for (int pass = 1; pass <= 2; ++pass) {
+                const int shift = pass == 1 ? 10 : 0;
+                const int nb = pass == 1 ? 2048 : 1024;
+                for (int i = tid; i < nb; i += BLOCK) hist[i] = 0;
+                __syncthreads();
+                for (int i = tid; i < nc; i += BLOCK) {
+                    const uint32_t key = cand_key[i];
+                    if ((key & pmask) == prefix)
+                        atomicAdd(&hist[(nb - 1) - ((key >> shift) & (nb - 1))], 1u);
+                }
+                __syncthreads();
+                block_find_desc<BLOCK>(hist, nb, krem, wtot, res);
+                prefix |= res[0] << shift;
+                pmask |= (uint32_t)(nb - 1) << shift;
+                krem = res[1];
+            }
+            for (int i = tid; i < nc; i += BLOCK)
+                if (cand_key[i] >= prefix) atomicAdd(&seg_cnt[(cand_pos[i] >> 2) / gseg], 1u);
+            __syncthreads();
+        } else {
+#pragma unroll 1
+            for (int pass = 1; pass <= 2; ++pass) {
+                const int shift = pass == 1 ? 10 : 0;
+                const int nb = pass == 1 ? 2048 : 1024;
+                for (int i = tid; i < nb; i += BLOCK) hist[i] = 0;
+                __syncthreads();
+                for (int g = tid; g < g4; g += BLOCK) {
+                    const uint4 kk = dyn4[g];
+                    const uint32_t e[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (4 * g + j < valid && (e[j] & pmask) == prefix)
+                            atomicAdd(&hist[(nb - 1) - ((e[j] >> shift) & (nb - 1))], 1u);
+                }
+                __syncthreads();
+                block_find_desc<BLOCK>(hist, nb, krem, wtot, res);
+                prefix |= res[0] << shift;
+                pmask |= (uint32_t)(nb - 1) << shift;
+                krem = res[1];
+            }
+            uint32_t c = 0;
+            for (int g = gs0 + lane; g < gs1; g += 32) {
+                const uint4 kk = dyn4[g];
+                c += (kk.x >= prefix) + (kk.y >= prefix) + (kk.z >= prefix) + (kk.w >= prefix);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+            if (lane == 0) seg_cnt[warp] = c;
+            __syncthreads();
+        }
+        const uint32_t thr_key = prefix;
+
+        // ---- sweep 3: ordered emission
+        uint32_t base = 0, tot = 0;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const uint32_t x = seg_cnt[w];
+            base += w < warp ? x : 0u;
+            tot += x;
+        }
+        if (tid == 0) {
+            a.thr[row] = key2f(thr_key);
+            if (a.cnt) a.cnt[row] = (int32_t)tot;
+        }
+        if (a.idx) {
+            int32_t* out = a.idx + row * a.idx_cap;
+            const uint32_t cap = (uint32_t)a.idx_cap;
+            for (int gb = gs0; gb < gs1 && base < cap; gb += 32) {
+                const int g = gb + lane;
+                const uint4 kk = g < gs1 ? dyn4[g] : make_uint4(0, 0, 0, 0);
+                const bool p0 = kk.x >= thr_key, p1 = kk.y >= thr_key, p2 = kk.z >= thr_key,
+                           p3 = kk.w >= thr_key;
+                const uint32_t n = p0 + p1 + p2 + p3;
+                uint32_t pre = n;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, pre, o);
+                    if (lane >= o) pre += y;
+                }
+                uint32_t pos = base + pre - n;
+                if (p0 && pos < cap) out[pos] = 4 * g;
+                pos += p0;
+                if (p1 && pos < cap) out[pos] = 4 * g + 1;
+                pos += p1;
+                if (p2 && pos < cap) out[pos] = 4 * g + 2;
+                pos += p2;
+                if (p3 && pos < cap) out[pos] = 4 * g + 3;
+                base += __shfl_sync(0xffffffffu, pre, 31);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+template <int BLOCK>
+int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream) {
+    a.cache_elems = (int)((longest + 3) & ~int64_t(3));
+    const int64_t cm = longest / 4;
+    a.cand_max = (int)(cm < 256 ? 256 : cm > 4096 ? 4096 : cm);
+    const size_t smem = ((size_t)a.cache_elems + 2 * (size_t)a.cand_max) * sizeof(uint32_t);
+    auto kern = topk_cached_kernel<BLOCK>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return fail(DSA_ERR_CUDA, "topk_select: cannot set dynamic shared memory size");
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, BLOCK, smem) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    int64_t grid = (int64_t)num_sms() * per_sm;
+    if (grid > a.n_rows) grid = a.n_rows;
+    kern<<<(unsigned)grid, BLOCK, smem, stream>>>(a);
+    return check_launch("topk_cached_kernel");
+}
+
 }  // namespace
 
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
@@ -245,6 +567,11 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     }
     constexpr int64_t kCacheMax = 12288;  // 48 KB of keys per CTA
     a.cache_elems = (int)(longest < kCacheMax ? longest : kCacheMax);
+    if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
+        if (longest <= 2048) return launch_cached<128>(a, longest, stream);
+        if (longest <= 8192) return launch_cached<256>(a, longest, stream);
+        return launch_cached<512>(a, longest, stream);
+    }
     if (longest <= 4096) return launch_topk<256>(a, stream);
     if (longest <= 16384) return launch_topk<512>(a, stream);
     return launch_topk<1024>(a, stream);

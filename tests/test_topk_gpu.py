@@ -119,3 +119,16 @@ def test_c2_full_size_properties(cuda):
     assert np.array_equal(thr[pick].cpu().numpy(), othr)
     for j, r in enumerate(pick.tolist()):
         assert np.array_equal(idx[r, : ocnt[j]].cpu().numpy(), oidx[j, : ocnt[j]])
+
+
+@pytest.mark.parametrize("N,k", [(2048, 128), (9000, 512), (20000, 2048)])
+def test_long_row_kernel_exact(cuda, N, k, monkeypatch):
+    """The kernel for rows longer than the shared-memory cache, forced on
+    shorter rows, gives the same exact result."""
+    monkeypatch.setenv("DSA_TOPK_LONG_PATH", "1")
+    g = torch.Generator().manual_seed(N + k)
+    x = torch.randn(6, N, generator=g)
+    x[0, ::2] = 0.0
+    assert_same(x, k)
+    s = torch.randn(2, 50, N, generator=g)
+    assert_same(s, k, causal=True, q_row0=N - 40)
