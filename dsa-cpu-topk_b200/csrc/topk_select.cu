@@ -290,7 +290,26 @@ __device__ __forceinline__ void block_find_desc(const uint32_t* hist, int nbins,
     __syncthreads();
 }
 
-template <int BLOCK>
+// Keys of group g (4 positions) of a row: from the shared cache, or (for rows
+// kept out of shared memory) re-read from L2; positions >= valid give key 0.
+template <bool CACHED>
+__device__ __forceinline__ uint4 group_keys(const uint4* cache4, const float* src, int g, int valid,
+                                            int vec_ok) {
+    if constexpr (CACHED) {
+        return cache4[g];
+    } else {
+        if (vec_ok && 4 * g + 3 < valid) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(src) + g);
+            return make_uint4(f2key(v.x), f2key(v.y), f2key(v.z), f2key(v.w));
+        }
+        uint32_t e[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
+        return make_uint4(e[0], e[1], e[2], e[3]);
+    }
+}
+
+template <int BLOCK, bool CACHED>
 __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
     constexpr int NW = BLOCK / 32;
     constexpr int S0 = 21;  // shift of the first digit
@@ -301,6 +320,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
     __shared__ __align__(16) uint32_t hist[NB_TOP];
     __shared__ uint32_t wtot[NW];
     __shared__ uint32_t seg_cnt[NW];
+    __shared__ uint32_t seg_base[NW + 1];
     __shared__ uint32_t res[2];
     __shared__ uint32_t n_cand;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -330,26 +350,38 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
         if (tid == 0) n_cand = 0;
         __syncthreads();
         if (a.vec_ok) {
+            // full groups, eight float4 loads in flight per thread
             const float4* src4 = reinterpret_cast<const float4*>(src);
-            for (int g = tid; g < g4; g += BLOCK) {
-                uint4 kk;
-                if (4 * g + 3 < valid) {
-                    const float4 v = __ldg(src4 + g);
-                    kk = make_uint4(f2key(v.x), f2key(v.y), f2key(v.z), f2key(v.w));
-                    atomicAdd(&hist[(NB_TOP - 1) - (kk.x >> S0)], 1u);
-                    atomicAdd(&hist[(NB_TOP - 1) - (kk.y >> S0)], 1u);
-                    atomicAdd(&hist[(NB_TOP - 1) - (kk.z >> S0)], 1u);
-                    atomicAdd(&hist[(NB_TOP - 1) - (kk.w >> S0)], 1u);
-                } else {
-                    uint32_t e[4];
+            const int gfull = valid >> 2;
+            constexpr int PIPE = 8;
+            for (int g0 = tid; g0 < gfull; g0 += PIPE * BLOCK) {
+                float4 v[PIPE];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
-                        if (4 * g + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
-                    }
-                    kk = make_uint4(e[0], e[1], e[2], e[3]);
+                for (int u = 0; u < PIPE; ++u) {
+                    const int g = g0 + u * BLOCK;
+                    v[u] = g < gfull ? __ldg(src4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                dyn4[g] = kk;
+#pragma unroll
+                for (int u = 0; u < PIPE; ++u) {
+                    const int g = g0 + u * BLOCK;
+                    if (g < gfull) {
+                        const uint4 kk = make_uint4(f2key(v[u].x), f2key(v[u].y), f2key(v[u].z), f2key(v[u].w));
+                        atomicAdd(&hist[(NB_TOP - 1) - (kk.x >> S0)], 1u);
+                        atomicAdd(&hist[(NB_TOP - 1) - (kk.y >> S0)], 1u);
+                        atomicAdd(&hist[(NB_TOP - 1) - (kk.z >> S0)], 1u);
+                        atomicAdd(&hist[(NB_TOP - 1) - (kk.w >> S0)], 1u);
+                        if (CACHED) dyn4[g] = kk;
+                    }
+                }
+            }
+            if (gfull < g4 && tid == BLOCK - 1) {  // the partial last group
+                uint32_t e[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    e[j] = 4 * gfull + j < valid ? f2key(__ldg(src + 4 * gfull + j)) : 0u;
+                    if (4 * gfull + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
+                }
+                if (CACHED) dyn4[gfull] = make_uint4(e[0], e[1], e[2], e[3]);
             }
         } else {
             for (int g = tid; g < g4; g += BLOCK) {
@@ -359,7 +391,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
                     e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
                     if (4 * g + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
                 }
-                dyn4[g] = make_uint4(e[0], e[1], e[2], e[3]);
+                if (CACHED) dyn4[g] = make_uint4(e[0], e[1], e[2], e[3]);
             }
         }
         __syncthreads();
@@ -380,7 +412,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
             uint32_t above = 0;
             for (int gb = gs0; gb < gs1; gb += 32) {
                 const int g = gb + lane;
-                uint4 kk = g < gs1 ? dyn4[g] : make_uint4(0, 0, 0, 0);
+                uint4 kk = g < gs1 ? group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
                 const uint32_t e[4] = {kk.x, kk.y, kk.z, kk.w};
                 uint32_t nin = 0;
 #pragma unroll
@@ -441,7 +473,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
                 for (int i = tid; i < nb; i += BLOCK) hist[i] = 0;
                 __syncthreads();
                 for (int g = tid; g < g4; g += BLOCK) {
-                    const uint4 kk = dyn4[g];
+                    const uint4 kk = group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok);
                     const uint32_t e[4] = {kk.x, kk.y, kk.z, kk.w};
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
@@ -456,7 +488,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
             }
             uint32_t c = 0;
             for (int g = gs0 + lane; g < gs1; g += 32) {
-                const uint4 kk = dyn4[g];
+                const uint4 kk = group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok);
                 c += (kk.x >= prefix) + (kk.y >= prefix) + (kk.z >= prefix) + (kk.w >= prefix);
             }
 #pragma unroll
@@ -466,14 +498,21 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
         }
         const uint32_t thr_key = prefix;
 
-        // ---- sweep 3: ordered emission
-        uint32_t base = 0, tot = 0;
+        // ---- sweep 3: ordered emission (warp 0 turns segment counts into offsets)
+        if (warp == 0) {
+            const uint32_t c = lane < NW ? seg_cnt[lane] : 0u;
+            uint32_t incl = c;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const uint32_t x = seg_cnt[w];
-            base += w < warp ? x : 0u;
-            tot += x;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (lane < NW) seg_base[lane] = incl - c;
+            if (lane == 31) seg_base[NW] = incl;
         }
+        __syncthreads();
+        uint32_t base = seg_base[warp];
+        const uint32_t tot = seg_base[NW];
         if (tid == 0) {
             a.thr[row] = key2f(thr_key);
             if (a.cnt) a.cnt[row] = (int32_t)tot;
@@ -483,7 +522,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
             const uint32_t cap = (uint32_t)a.idx_cap;
             for (int gb = gs0; gb < gs1 && base < cap; gb += 32) {
                 const int g = gb + lane;
-                const uint4 kk = g < gs1 ? dyn4[g] : make_uint4(0, 0, 0, 0);
+                const uint4 kk = g < gs1 ? group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
                 const bool p0 = kk.x >= thr_key, p1 = kk.y >= thr_key, p2 = kk.z >= thr_key,
                            p3 = kk.w >= thr_key;
                 const uint32_t n = p0 + p1 + p2 + p3;
@@ -508,13 +547,13 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
     }
 }
 
-template <int BLOCK>
+template <int BLOCK, bool CACHED>
 int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream) {
-    a.cache_elems = (int)((longest + 3) & ~int64_t(3));
+    a.cache_elems = CACHED ? (int)((longest + 3) & ~int64_t(3)) : 0;
     const int64_t cm = longest / 4;
     a.cand_max = (int)(cm < 256 ? 256 : cm > 4096 ? 4096 : cm);
     const size_t smem = ((size_t)a.cache_elems + 2 * (size_t)a.cand_max) * sizeof(uint32_t);
-    auto kern = topk_cached_kernel<BLOCK>;
+    auto kern = topk_cached_kernel<BLOCK, CACHED>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return fail(DSA_ERR_CUDA, "topk_select: cannot set dynamic shared memory size");
@@ -568,9 +607,12 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     constexpr int64_t kCacheMax = 12288;  // 48 KB of keys per CTA
     a.cache_elems = (int)(longest < kCacheMax ? longest : kCacheMax);
     if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
-        if (longest <= 2048) return launch_cached<128>(a, longest, stream);
-        if (longest <= 8192) return launch_cached<256>(a, longest, stream);
-        return launch_cached<512>(a, longest, stream);
+        if (longest <= 2048) return launch_cached<128, true>(a, longest, stream);
+        if (longest <= 8192) return launch_cached<256, true>(a, longest, stream);
+        // longer rows: the sweeps after the first re-read the row from L2, so
+        // several CTAs fit on an SM (DSA_TOPK_SMEM_ROWS=1 caches them instead)
+        if (getenv("DSA_TOPK_SMEM_ROWS")) return launch_cached<512, true>(a, longest, stream);
+        return launch_cached<256, false>(a, longest, stream);
     }
     if (longest <= 4096) return launch_topk<256>(a, stream);
     if (longest <= 16384) return launch_topk<512>(a, stream);
