@@ -140,6 +140,30 @@ DSA_API int dsa_forward(const void* q_idx, const void* k_idx, const float* w_idx
                 int idx_dtype, int qkv_dtype, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/*
+ * Whole forward with no allocation and no caller workspace.  No counterpart
+ * in the reference: it exists for callers that cannot allocate device memory
+ * where they run the forward (a host framework that owns all GPU memory
+ * through its own pool, a plugin that is only handed its input and output
+ * buffers), so they cannot provide dsa_forward's workspace.
+ *   Arguments as dsa_forward, minus workspace / workspace_bytes.
+ *   Scratch: a 32 MiB device array inside the library, reserved on every GPU
+ *   that loads the library until the process exits.  Shapes whose
+ *   dsa_forward_workspace_bytes(...) exceeds 32 MiB are rejected with
+ *   DSA_ERR_INVALID (e.g. B=16, T=512, top_k=32 fits; T=8192 does not).
+ *   The first call on a device looks up the array's device address for that
+ *   device (cudaGetSymbolAddress); make that first call before any stream
+ *   capture.  No cudaMalloc / cudaFree is ever called.
+ *   All calls on a device share the one array and nothing in it needs
+ *   clearing between calls; calls that overlap on the GPU (different streams,
+ *   or host threads without ordering) race on it and must be serialised.
+ */
+DSA_API int dsa_forward_noalloc(const void* q_idx, const void* k_idx, const float* w_idx,
+                                const void* Q, const void* K, const void* V, float* O,
+                                int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                                int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV,
+                                int64_t top_k, int idx_dtype, int qkv_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
