@@ -443,6 +443,22 @@ def run_b200(args, cfg, world, rank, local):
         line["gpu_launches"] += 3 * len(blocks) * args.steps
         del h_key, h_rows, d_key, d_rows, ws, h_out
 
+    # ---- verification (outside every timed region): gather the sharded rows over
+    # NCCL and compare them with rank 0's own single-GPU forward of the whole
+    # workload.  Both run the same kernels, so the rows must match bit for bit.
+    if args.verify and args.scaling == "strong":
+        from dsa_attention import dsa_forward as fwd_all
+        plan = sharding.zigzag_plan(T, world)
+        local_rows = torch.cat([p["O"] for p in pipe.parts], dim=1)
+        full = sharding.gather_rows(local_rows, plan) if world > 1 else local_rows
+        if rank == 0:
+            whole = fwd_all(*inputs, cfg["k"])
+            line["verify"] = {"rows": T, "max_abs_diff": float((full - whole).abs().max()),
+                              "bitwise_equal": bool(torch.equal(full, whole)),
+                              "gather": "NCCL all_gather of output rows" if world > 1 else "none (1 rank)"}
+    elif args.verify:
+        line["verify"] = {"skipped": "weak scaling: every rank computes whole sequences itself"}
+
     # ---- CPU baseline (rank 0 at N=1 only)
     if world == 1 and rank == 0 and not args.no_cpu:
         ctx = cpu_reference_setup(cfg, inputs)
@@ -501,6 +517,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-step-seconds", type=float, default=3.0)
+    ap.add_argument("--verify", action="store_true",
+                    help="after timing, gather the sharded output rows (NCCL) and compare with a "
+                         "single-GPU forward on rank 0 (strong scaling)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))
