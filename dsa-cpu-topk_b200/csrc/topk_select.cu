@@ -567,6 +567,157 @@ int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream) {
     return check_launch("topk_cached_kernel");
 }
 
+// ===========================================================================
+// Short rows (<= 512 entries: configs c1 and c3): one warp
+// per row, the row's keys in registers (NG float4 groups per lane), no block
+// barriers.  Four 8-bit radix passes over the register-resident keys use a
+// 256-bin histogram per warp (descending slots, scanned by the warp);
+// after the first pass only keys matching the selected prefix touch it.
+// Emission orders the kept positions with ballots.
+// ===========================================================================
+
+// NB1: bins of the first pass (256 -> 8+8+8+8 bits; 2048 -> 11+8+8+5 bits).
+template <int NG, int NB1>
+__global__ void __launch_bounds__(256) topk_warp_kernel(TopkArgs a) {
+    extern __shared__ uint4 wdyn[];  // 8 warps x NB1 bins
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(wdyn) + warp * NB1;
+    const uint32_t lt_mask = (1u << lane) - 1u;
+
+    for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.n_rows; row += (int64_t)gridDim.x * 8) {
+        const float* src = a.scores + row * a.row_stride;
+        int valid = (int)a.row_len;
+        if (a.causal) {
+            const int64_t t = a.q_row0 + row % a.rows_per_batch;
+            valid = t + 1 < a.row_len ? (int)(t + 1) : (int)a.row_len;
+        }
+        if (a.k > valid) {
+            if (lane == 0) {
+                a.thr[row] = __uint_as_float(0xff800000u);
+                if (a.cnt) a.cnt[row] = valid;
+            }
+            if (a.idx) {
+                const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
+                for (int i = lane; i < n; i += 32) a.idx[row * a.idx_cap + i] = i;
+            }
+            continue;
+        }
+        // ---- load: group g = lane + 32j holds positions 4g..4g+3; padding keys are 0
+        uint32_t key[NG][4];
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+            const int g = lane + 32 * j;
+            if (a.vec_ok && 4 * g + 3 < valid) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(src) + g);
+                key[j][0] = f2key(v.x); key[j][1] = f2key(v.y); key[j][2] = f2key(v.z); key[j][3] = f2key(v.w);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) key[j][e] = 4 * g + e < valid ? f2key(__ldg(src + 4 * g + e)) : 0u;
+            }
+        }
+        // ---- radix passes, most significant first
+        uint32_t prefix = 0, pmask = 0, krem = (uint32_t)a.k;
+#pragma unroll 1
+        for (int pass = 0; pass < 4; ++pass) {
+            const int bits = pass == 0 ? (NB1 == 2048 ? 11 : 8) : (NB1 == 2048 && pass == 3 ? 5 : 8);
+            const int shift = NB1 == 2048 ? (pass == 0 ? 21 : pass == 1 ? 13 : pass == 2 ? 5 : 0) : 24 - 8 * pass;
+            const int nb = 1 << bits;
+            const int nbs = nb < 256 ? 256 : nb;  // slots scanned (unused ones stay 0)
+            const int per = nbs / 32;              // slots per lane: 8 or 64
+            for (int i = lane * 4; i < nbs; i += 128) *reinterpret_cast<uint4*>(hist + i) = make_uint4(0, 0, 0, 0);
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < NG; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (4 * (lane + 32 * j) + e < valid && (key[j][e] & pmask) == prefix)
+                        atomicAdd(&hist[(nbs - 1) - ((key[j][e] >> shift) & (uint32_t)(nb - 1))], 1u);
+            __syncwarp();
+            // lane owns slots [per*lane, per*lane+per) (descending digits)
+            uint32_t local = 0;
+            for (int i = 0; i < per; i += 4) {
+                const uint4 h = *reinterpret_cast<const uint4*>(hist + lane * per + i);
+                local += h.x + h.y + h.z + h.w;
+            }
+            uint32_t incl = local;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t excl = incl - local;
+            const bool mine = excl < krem && krem <= incl;
+            uint32_t dig = 0, kr = 0;
+            if (mine) {
+                uint32_t c = excl;
+                for (int i = 0; i < per; ++i) {
+                    const uint32_t h = hist[lane * per + i];
+                    if (krem <= c + h) {
+                        dig = (uint32_t)(nbs - 1 - (lane * per + i)) + 1u;  // +1: 0 marks "not found"
+                        kr = krem - c;
+                        break;
+                    }
+                    c += h;
+                }
+            }
+            const uint32_t who = __ballot_sync(0xffffffffu, mine);
+            const int src_lane = who ? __ffs(who) - 1 : 0;
+            dig = __shfl_sync(0xffffffffu, dig, src_lane);
+            kr = __shfl_sync(0xffffffffu, kr, src_lane);
+            prefix |= (dig - 1u) << shift;
+            pmask |= (uint32_t)(nb - 1) << shift;
+            krem = kr;
+            __syncwarp();
+        }
+        const uint32_t thr_key = prefix;
+
+        // ---- count and ordered emission
+        uint32_t base = 0;
+        int32_t* out = a.idx ? a.idx + row * a.idx_cap : nullptr;
+        const uint32_t cap = (uint32_t)a.idx_cap;
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+            const int g = lane + 32 * j;
+            bool pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pk[e] = 4 * g + e < valid && key[j][e] >= thr_key;
+            const uint32_t m0 = __ballot_sync(0xffffffffu, pk[0]), m1 = __ballot_sync(0xffffffffu, pk[1]),
+                           m2 = __ballot_sync(0xffffffffu, pk[2]), m3 = __ballot_sync(0xffffffffu, pk[3]);
+            if (out) {
+                uint32_t pos = base + __popc(m0 & lt_mask) + __popc(m1 & lt_mask) + __popc(m2 & lt_mask) +
+                               __popc(m3 & lt_mask);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (pk[e]) {
+                        if (pos < cap) out[pos] = 4 * g + e;
+                        ++pos;
+                    }
+            }
+            base += __popc(m0) + __popc(m1) + __popc(m2) + __popc(m3);
+        }
+        if (lane == 0) {
+            a.thr[row] = key2f(thr_key);
+            if (a.cnt) a.cnt[row] = (int32_t)base;
+        }
+    }
+}
+
+template <int NG, int NB1>
+int launch_warp(const TopkArgs& a, cudaStream_t stream) {
+    auto kern = topk_warp_kernel<NG, NB1>;
+    const size_t smem = 8 * NB1 * sizeof(uint32_t);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return fail(DSA_ERR_CUDA, "topk_select: cannot set dynamic shared memory size");
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    int64_t grid = (int64_t)num_sms() * per_sm;
+    const int64_t need = (a.n_rows + 7) / 8;
+    if (grid > need) grid = need;
+    kern<<<(unsigned)grid, 256, smem, stream>>>(a);
+    return check_launch("topk_warp_kernel");
+}
+
 }  // namespace
 
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
@@ -606,6 +757,13 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     }
     constexpr int64_t kCacheMax = 12288;  // 48 KB of keys per CTA
     a.cache_elems = (int)(longest < kCacheMax ? longest : kCacheMax);
+    // rows <= 512: one warp per row (measured 2.6-2.9x faster than a CTA per
+    // row there; slower than it on 1K-2K rows, where the CTA kernel is kept)
+    if (longest <= 512 && !getenv("DSA_TOPK_LONG_PATH") && !getenv("DSA_TOPK_NO_WARP")) {
+        if (longest <= 128) return launch_warp<1, 256>(a, stream);
+        if (longest <= 256) return launch_warp<2, 256>(a, stream);
+        return launch_warp<4, 256>(a, stream);
+    }
     if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
         if (longest <= 2048) return launch_cached<128, true>(a, longest, stream);
         if (longest <= 8192) return launch_cached<256, true>(a, longest, stream);

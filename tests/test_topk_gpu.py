@@ -132,3 +132,16 @@ def test_long_row_kernel_exact(cuda, N, k, monkeypatch):
     assert_same(x, k)
     s = torch.randn(2, 50, N, generator=g)
     assert_same(s, k, causal=True, q_row0=N - 40)
+
+
+@pytest.mark.parametrize("N,k", [(100, 7), (512, 32), (512, 512), (300, 128)])
+def test_block_kernel_on_short_rows_exact(cuda, N, k, monkeypatch):
+    """Rows <= 512 normally run one warp per row; the CTA-per-row kernel,
+    forced on them, gives the same exact result."""
+    monkeypatch.setenv("DSA_TOPK_NO_WARP", "1")
+    g = torch.Generator().manual_seed(N * 3 + k)
+    x = torch.randn(40, N, generator=g)
+    x[3] = torch.round(x[3])
+    assert_same(x, k)
+    s = torch.randn(3, 64, N, generator=g)
+    assert_same(s, min(k, N), causal=True, q_row0=max(0, N - 70))
