@@ -48,6 +48,7 @@ CONFIGS = {
                desc="DSA fwd B1 T32768 k2048 HI64 DI128 HQ16 D128 bf16, causal (DeepSeek-V3.2 scale)"),
 }
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+C2 = dict(B=64, T=2048, k=128, desc="top-K only: fp32 scores 64 x 2048 x 2048, N(0,1), s > t = -inf, k=128")
 
 
 def load_peaks():
@@ -498,6 +499,67 @@ def run_b200(args, cfg, world, rank, local):
     return line
 
 
+def run_topk_only(args, world, rank, local):
+    """Config c2: stage 2 alone, rows/s (one row = one query's 2048 scores)."""
+    import _native
+    from topk import idx_cap_for
+    dev = torch.device("cuda", local)
+    B, T, k = C2["B"], C2["T"], C2["k"]
+    g = torch.Generator(device=dev).manual_seed(1000 * rank)
+    s = torch.randn((B, T, T), generator=g, device=dev)
+    s.masked_fill_(~torch.ones(T, T, device=dev, dtype=torch.bool).tril(), float("-inf"))
+    rows = B * T
+    cap = idx_cap_for(k, T)
+    thr = torch.empty(rows, device=dev)
+    cnt = torch.empty(rows, device=dev, dtype=torch.int32)
+    idx = torch.empty((rows, cap), device=dev, dtype=torch.int32)
+    flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream()
+    res = {}
+    for mode in ("full", "causal"):
+        def step():
+            _native.topk_select(s, rows, T, T, k, thr, idx, cnt, cap, causal=(mode == "causal"),
+                                rows_per_batch=T)
+        for _ in range(args.warmup):
+            step()
+        barrier(world)
+        tot = 0.0
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(args.steps):
+            flush.zero_()
+            st.record(stream); step(); en.record(stream); en.synchronize()
+            tot += st.elapsed_time(en)
+        ms = max_over_ranks(tot, world) / args.steps
+        read = rows * T * 4 if mode == "full" else B * T * (T + 1) / 2 * 4
+        written = rows * 8 + cnt.double().sum().item() * 4
+        res[mode] = dict(ms=ms, rows_per_s=world * rows / (ms / 1e3), gbs=(read + written) / (ms / 1e3) / 1e9)
+    hbm, _, src = load_peaks()
+    line = {"metric": "top-K rows/s (per-row k-th largest + kept-index list)", "value": res["full"]["rows_per_s"],
+            "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["full"]["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": f"c2: {C2['desc']}",
+                                                             "l2": "L2 flushed between steps (256 MB write)"},
+            "roofline": {"bound": "hbm", "achieved": res["full"]["gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": res["full"]["gbs"] / hbm, "traffic": None, "kernel": "topk_select"},
+            "causal_mode": res["causal"], "gpu_launches": 2 * (args.steps + args.warmup)}
+    if world == 1 and not args.no_cpu:
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import build_ref
+        ext = build_ref.load_ref()
+        sample = s[:4].cpu().contiguous()                      # 8192 rows
+        f = (lambda x: ext.topk_threshold(x, k)) if ext else (lambda x: x.topk(k, -1).values[..., -1:])
+        f(sample)
+        t0 = time.perf_counter(); n = 0
+        while time.perf_counter() - t0 < args.cpu_seconds:
+            f(sample); n += 1
+        el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": n * sample.shape[0] * T / el, "unit": "rows/s",
+                                "cores": torch.get_num_threads(),
+                                "kind": "reference" if ext else "port",
+                                "sample": f"{n} x 8192 rows of 2048 (threshold only, as topk_threshold) in {el:.1f} s"}
+    return line
+
+
 def run_reference(args, cfg, world, rank, local):
     """The reference's own CPU implementation of the path on this host's cores."""
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
@@ -540,7 +602,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS) + ["c2"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -551,8 +613,18 @@ def main():
                     help="after timing, gather the sharded output rows (NCCL) and compare with a "
                          "single-GPU forward on rank 0 (strong scaling)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = CONFIGS.get(args.config)
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.config == "c2":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "c2 is a top-K-only config; its CPU "
+                              "baseline is reported in the b200 arm's cpu_baseline"}), flush=True)
+            return
+        world, rank, local = dist_setup()
+        line = run_topk_only(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         if rank != 0:
