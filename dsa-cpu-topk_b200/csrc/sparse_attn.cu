@@ -281,6 +281,155 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Small heads (a team of L = HQ*G <= 32 threads, L a power of two: configs
+// c1-c3): one warp per query row, eight rows per CTA, no block barriers.  The
+// warp's 32/L teams split the key list and merge with xor-shuffles.  Key
+// indices arrive 32 at a time (one per lane) and are handed out by shuffle.
+// ---------------------------------------------------------------------------
+template <typename T, int C, int G, int U>
+__global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
+    constexpr int VEC = 16 / sizeof(T);
+    constexpr int NP = C * VEC / 2;
+    constexpr int PP = Pairs<T>::PER16;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= a.B * a.T_q) return;  // warp-uniform
+    const int L = a.HQ * G;
+    const int P = 32 / L;
+    const int team = lane / L;
+    const int lt = lane - team * L;
+    const int64_t b = row / a.T_q;
+    const int64_t t = a.q_row0 + (row - b * a.T_q);
+    const int64_t valid = t + 1 < a.T_k ? t + 1 : a.T_k;
+    const int64_t rowlen = (int64_t)a.HQ * a.D;
+    const int64_t toff = (int64_t)(lt / G) * a.D + (lt % G) * VEC;
+    const T* Kb = a.K + b * a.T_k * rowlen + toff;
+    const T* Vb = a.V + b * a.T_k * rowlen + toff;
+
+    float2 q[NP], acc[NP];
+    {
+        const T* qp = a.Q + row * rowlen + toff;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const uint4 v = ldg16(qp + c * G * VEC);
+#pragma unroll
+            for (int i = 0; i < PP; ++i) {
+                const float2 f = Pairs<T>::get(v, i);
+                q[c * PP + i] = make_float2(f.x * a.scale_log2, f.y * a.scale_log2);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < NP; ++i) acc[i] = make_float2(0.f, 0.f);
+    }
+    float m = kNegInf, l = 0.f;
+
+    bool list_mode = false;
+    int64_t n_total = valid;
+    if (a.idx) {
+        const int64_t c = a.cnt[row];
+        if (c <= a.idx_cap) {
+            list_mode = true;
+            n_total = c;
+        }
+    }
+    const float thr = list_mode ? 0.f : a.thr[row];
+    const float* srow = list_mode ? nullptr : a.scores + row * a.T_k;
+
+    for (int64_t c0 = 0; c0 < n_total; c0 += 32) {
+        // this chunk's keys: lane r holds the r-th one
+        int mykey = 0, n;
+        if (list_mode) {
+            n = (int)(n_total - c0 < 32 ? n_total - c0 : 32);
+            if (lane < n) mykey = __ldg(a.idx + row * a.idx_cap + c0 + lane);
+        } else {
+            const int64_t s = c0 + lane;
+            const uint32_t bal = __ballot_sync(0xffffffffu, s < n_total && __ldg(srow + s) >= thr);
+            n = __popc(bal);
+            if (lane < n) mykey = (int)c0 + (int)__fns(bal, 0, lane + 1);
+        }
+        for (int base = 0; base < n; base += P * U) {
+            uint4 kr[U][C], vr[U][C];
+            bool ok[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int j = base + team + u * P;
+                ok[u] = j < n;
+                const int s = __shfl_sync(0xffffffffu, mykey, j & 31);
+                const int64_t off = (int64_t)(ok[u] ? s : 0) * rowlen;
+#pragma unroll
+                for (int c = 0; c < C; ++c) {
+                    kr[u][c] = ok[u] ? ldg16(Kb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                    vr[u][c] = ok[u] ? ldg16(Vb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                }
+            }
+            float x[U];
+            float mx = kNegInf;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float2 d2 = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+#pragma unroll
+                    for (int i = 0; i < PP; ++i) d2 = ffma2(q[c * PP + i], Pairs<T>::get(kr[u][c], i), d2);
+                float d = d2.x + d2.y;
+#pragma unroll
+                for (int o = G / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                x[u] = ok[u] ? d : kNegInf;
+                mx = fmaxf(mx, x[u]);
+            }
+            if (mx > m + kRescale) {
+                const float corr = exp2f(m - mx);
+                const float2 c2 = make_float2(corr, corr);
+                l *= corr;
+#pragma unroll
+                for (int i = 0; i < NP; ++i) acc[i] = fmul2(acc[i], c2);
+                m = mx;
+            }
+            if (m == kNegInf) continue;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float p = exp2f(x[u] - m);
+                l += p;
+                const float2 p2 = make_float2(p, p);
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+#pragma unroll
+                    for (int i = 0; i < PP; ++i)
+                        acc[c * PP + i] = ffma2(p2, Pairs<T>::get(vr[u][c], i), acc[c * PP + i]);
+            }
+        }
+    }
+    // merge the warp's teams
+    for (int off = L; off < 32; off <<= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+        const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
+        const float mx = fmaxf(m, m2);
+        const float f1 = m == kNegInf ? 0.f : exp2f(m - mx);
+        const float f2 = m2 == kNegInf ? 0.f : exp2f(m2 - mx);
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+            const float ax = __shfl_xor_sync(0xffffffffu, acc[i].x, off);
+            const float ay = __shfl_xor_sync(0xffffffffu, acc[i].y, off);
+            acc[i] = make_float2(acc[i].x * f1 + ax * f2, acc[i].y * f1 + ay * f2);
+        }
+        l = l * f1 + l2 * f2;
+        m = mx;
+    }
+    if (team == 0) {
+        float* orow = a.O + row * rowlen + toff;
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+#pragma unroll
+            for (int i = 0; i < PP; i += 2) {
+                const float2 x0 = acc[c * PP + i], x1 = acc[c * PP + i + 1];
+                *reinterpret_cast<float4*>(orow + c * G * VEC + 2 * i) =
+                    make_float4(x0.x * inv, x0.y * inv, x1.x * inv, x1.y * inv);
+            }
+    }
+}
+
 template <typename T, int C, int G>
 int launch_g(const AttnArgs<T>& a, cudaStream_t stream) {
     constexpr int VEC = 16 / sizeof(T);
@@ -293,6 +442,10 @@ int launch_g(const AttnArgs<T>& a, cudaStream_t stream) {
     else if (L <= 512) block = 512;
     else if (L <= 1024) block = 1024;
     else return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: HQ*D too large for one CTA per key row");
+    if (L <= 32 && (L & (L - 1)) == 0 && !getenv("DSA_ATTN_NO_WARP")) {
+        sparse_attn_warp_kernel<T, C, G, 2><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(a);
+        return check_launch("sparse_attn_warp_kernel");
+    }
     const int P = block / L;
     const size_t smem = P == 1 ? 0 : (size_t)(2 * P * a.HQ + P * L * E) * sizeof(float);
 #define DSA_LAUNCH(BLK, UU, MB)                                                                   \

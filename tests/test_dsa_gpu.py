@@ -113,3 +113,19 @@ def test_row_sharded_forward_equals_whole(cuda):
     parts = [dsa_forward(qi[:, a:b], ki, wi[:, a:b], Q[:, a:b], K, V, 64, q_row0=a)
              for a, b in [(0, 100), (100, 333), (333, 640)]]
     assert torch.equal(torch.cat(parts, 1), whole)
+
+
+@pytest.mark.parametrize("name", ["dsa_T128_k32", "dsa_T200_k24", "dsa_c1_B1"])
+def test_block_attention_kernel_on_small_heads(cuda, name, monkeypatch):
+    """Small heads normally run one warp per query row; the CTA-per-row
+    kernel, forced on them, gives the same result."""
+    from dsa_attention import dsa_attention_split_triton
+    d = golden(name)
+    args, dt = inputs(d, cuda)
+    k = int(d["top_k"])
+    warp_out = dsa_attention_split_triton(*args, top_k=k).cpu()
+    monkeypatch.setenv("DSA_ATTN_NO_WARP", "1")
+    block_out = dsa_attention_split_triton(*args, top_k=k).cpu()
+    ref = t(d["out"])
+    assert (block_out - ref).abs().max() < 5e-4
+    assert (warp_out - block_out).abs().max() < 1e-5
