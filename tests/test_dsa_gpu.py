@@ -129,3 +129,27 @@ def test_block_attention_kernel_on_small_heads(cuda, name, monkeypatch):
     ref = t(d["out"])
     assert (block_out - ref).abs().max() < 5e-4
     assert (warp_out - block_out).abs().max() < 1e-5
+
+
+@pytest.mark.parametrize("B,T,HI,DI,HQ,D,k,dtype", [
+    (16, 512, 4, 32, 4, 32, 32, torch.float32),     # config c1
+    (2, 300, 3, 24, 2, 32, 40, torch.float32),      # ragged T, odd HI/DI
+    (1, 77, 2, 16, 2, 16, 80, torch.float32),       # k > T
+    (2, 512, 4, 64, 8, 64, 64, torch.bfloat16),
+    (1, 128, 8, 128, 4, 16, 16, torch.float16),
+])
+def test_fused_small_matches_three_stage_pipeline(cuda, B, T, HI, DI, HQ, D, k, dtype, monkeypatch):
+    """The opt-in one-launch kernel for short sequences must agree with the
+    three-stage pipeline (same fp32 score arithmetic, so the same kept sets)."""
+    from dsa_attention import dsa_forward
+    args = [x.to(cuda) for x in o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype)]
+    kk = min(k, T)
+    staged = dsa_forward(*args, kk).cpu()
+    monkeypatch.setenv("DSA_FUSED_SMALL", "1")
+    fused = dsa_forward(*args, kk).cpu()
+    tol = 1e-5 if dtype == torch.float32 else 1e-3
+    assert (fused - staged).abs().max() <= tol * max(1.0, staged.abs().max().item())
+    if dtype == torch.float32:
+        ref = o.dsa_attention(*[x.cpu() for x in args], k)
+        bad = ((fused - ref).abs() > 1e-3 + 1e-3 * ref.abs()).any(-1).any(-1)
+        assert bad.float().mean() < 0.002
