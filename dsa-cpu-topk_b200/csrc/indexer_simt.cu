@@ -16,6 +16,7 @@
 // entirely above the causal diagonal do no math (they are filled with -inf
 // only when the caller asks for the full matrix).
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -129,6 +130,122 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
     }
 }
 
+// Small heads (HI*DI <= 256): the tile's q rows of every head and its key
+// rows are staged once (one barrier), then all heads are computed from
+// shared memory.  Same per-(t,s) arithmetic and order as the kernel above.
+template <typename T, bool V4>
+__global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __restrict__ q,
+                                                                const T* __restrict__ k,
+                                                                const float* __restrict__ w,
+                                                                float* __restrict__ scores,
+                                                                int64_t T_q, int64_t T_k,
+                                                                int64_t q_row0, int HI, int DI,
+                                                                int fill_upper) {
+    extern __shared__ __align__(16) float sm[];
+    // row strides in floats: q rows are read as broadcasts, key rows by 16
+    // lanes at once (stride DI+1 spreads them over distinct banks)
+    // (V4: float4 reads along d, strides kept multiples of 4)
+    const int QS = HI * DI + 4, KS = V4 ? DI + 4 : DI + 1;
+    float* qs = sm;                            // [BT][QS]
+    float* ks = sm + BT * QS;                  // [BS][KS]
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int64_t b = blockIdx.z;
+    const int64_t tq0 = (int64_t)blockIdx.y * BT;
+    const int64_t s0 = (int64_t)blockIdx.x * BS;
+    const int64_t tq_end = tq0 + BT < T_q ? tq0 + BT : T_q;
+    const int64_t t_max = q_row0 + tq_end - 1;
+    float* srow0 = scores + (b * T_q) * T_k;
+    const float NEG = -INFINITY;
+    if (s0 > t_max) {
+        if (fill_upper) {
+            for (int e = tid; e < BT * BS; e += 256) {
+                const int64_t tq = tq0 + e / BS, s = s0 + e % BS;
+                if (tq < T_q && s < T_k) srow0[tq * T_k + s] = NEG;
+            }
+        }
+        return;
+    }
+    const int HD = HI * DI;
+    const T* qb = q + (b * T_q + tq0) * (int64_t)HD;
+    const T* kb = k + (b * T_k + s0) * (int64_t)DI;
+    for (int e = tid; e < BT * HD; e += 256) {
+        const int r = e / HD, c = e - r * HD;
+        qs[r * QS + c] = tq0 + r < T_q ? Elem<T>::to_f(qb[e]) : 0.f;
+    }
+    for (int e = tid; e < BS * DI; e += 256) {
+        const int r = e / DI, c = e - r * DI;
+        ks[r * KS + c] = s0 + r < T_k ? Elem<T>::to_f(kb[e]) : 0.f;
+    }
+    __syncthreads();
+
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj] = 0.f;
+    for (int j = 0; j < HI; ++j) {
+        float dot[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) dot[i][jj] = 0.f;
+        if constexpr (V4) {
+            for (int d = 0; d < DI; d += 4) {
+                float4 a4[4], b4[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    a4[i] = *reinterpret_cast<const float4*>(&qs[(ty + 16 * i) * QS + j * DI + d]);
+                    b4[i] = *reinterpret_cast<const float4*>(&ks[(tx + 16 * i) * KS + d]);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        float x = dot[i][jj];
+                        x = fmaf(a4[i].x, b4[jj].x, x);
+                        x = fmaf(a4[i].y, b4[jj].y, x);
+                        x = fmaf(a4[i].z, b4[jj].z, x);
+                        x = fmaf(a4[i].w, b4[jj].w, x);
+                        dot[i][jj] = x;
+                    }
+            }
+        } else {
+            for (int d = 0; d < DI; ++d) {
+                float av[4], bv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    av[i] = qs[(ty + 16 * i) * QS + j * DI + d];
+                    bv[i] = ks[(tx + 16 * i) * KS + d];
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) dot[i][jj] = fmaf(av[i], bv[jj], dot[i][jj]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t tq = tq0 + ty + 16 * i;
+            const float wv = tq < T_q ? w[(b * T_q + tq) * HI + j] : 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(wv, fmaxf(dot[i][jj], 0.f), acc[i][jj]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t tq = tq0 + ty + 16 * i;
+        if (tq >= T_q) continue;
+        const int64_t t = q_row0 + tq;
+        float* out = srow0 + tq * T_k;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int64_t s = s0 + tx + 16 * jj;
+            if (s < T_k) out[s] = s <= t ? acc[i][jj] : NEG;
+        }
+    }
+}
+
 template <typename T>
 int launch(const void* q, const void* k, const float* w, float* scores, int64_t B, int64_t T_q,
            int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI, int fill_upper,
@@ -137,6 +254,16 @@ int launch(const void* q, const void* k, const float* w, float* scores, int64_t 
     if (gx > INT32_MAX || gy > 65535 || B > 65535)
         return fail(DSA_ERR_INVALID, "indexer: grid too large (T_q/64 and B must be <= 65535)");
     dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)B);
+    if (HI * DI <= 256 && !getenv("DSA_INDEXER_SIMT_GENERIC")) {
+        const bool v4 = DI % 4 == 0;
+        const size_t smem = ((size_t)BT * (HI * DI + 4) + (size_t)BS * (DI + (v4 ? 4 : 1))) * sizeof(float);
+        auto kern = v4 ? indexer_simt_small_kernel<T, true> : indexer_simt_small_kernel<T, false>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return fail(DSA_ERR_CUDA, "indexer: cannot set dynamic shared memory size");
+        kern<<<grid, 256, smem, stream>>>((const T*)q, (const T*)k, w, scores, T_q, T_k, q_row0, (int)HI,
+                                          (int)DI, fill_upper);
+        return check_launch("indexer_simt_small_kernel");
+    }
     indexer_simt_kernel<T><<<grid, 256, 0, stream>>>((const T*)q, (const T*)k, w, scores, T_q, T_k,
                                                      q_row0, (int)HI, (int)DI, fill_upper);
     return check_launch("indexer_simt_kernel");

@@ -76,3 +76,17 @@ def test_row_offset_and_fill(cuda):
     out2 = indexer_scores(qi.to(cuda), ki.to(cuda), wi.to(cuda), fill_upper=False).cpu()
     causal = torch.ones(300, 300, dtype=torch.bool).tril()
     assert torch.allclose(out2[:, causal], full[:, causal], rtol=1e-3, atol=1e-4)
+
+
+@pytest.mark.parametrize("B,T,HI,DI,dtype", [(4, 512, 4, 32, torch.float32), (2, 333, 3, 48, torch.float32),
+                                             (1, 200, 8, 32, torch.bfloat16), (2, 130, 2, 7, torch.float32)])
+def test_small_head_simt_kernel_bitwise(cuda, B, T, HI, DI, dtype, monkeypatch):
+    """The staged-once kernel for small heads gives the same fp32 bits as the
+    generic CUDA-core kernel (same products, same summation order)."""
+    from lightning_indexer import indexer_scores
+    qi, ki, wi, *_ = (x.to(cuda) for x in o.make_inputs(B, T, HI, DI, 1, 16, 16, dtype=dtype))
+    monkeypatch.setenv("DSA_FORCE_SIMT_INDEXER", "1")
+    small = indexer_scores(qi, ki, wi)
+    monkeypatch.setenv("DSA_INDEXER_SIMT_GENERIC", "1")
+    generic = indexer_scores(qi, ki, wi)
+    assert torch.equal(small, generic)
