@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdsa_b200.so")
 
-DSA_OK, DSA_ERR_INVALID, DSA_ERR_UNSUPPORTED, DSA_ERR_CUDA = 0, -1, -2, -3
+DSA_OK, DSA_ERR_INVALID, DSA_ERR_UNSUPPORTED, DSA_ERR_CUDA, DSA_ERR_TIMEOUT = 0, -1, -2, -3, -4
 DSA_F32, DSA_BF16, DSA_F16 = 0, 1, 2
 _DTYPES = {torch.float32: DSA_F32, torch.bfloat16: DSA_BF16, torch.float16: DSA_F16}
 
@@ -41,6 +41,8 @@ def lib() -> ctypes.CDLL:
                                                 f32, i32, p]
         L.dsa_sparse_attn.argtypes = [p, p, i64, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
                                       f32, i32, p]
+        L.dsa_device_status.argtypes = [p]
+        L.dsa_device_status.restype = i32
         L.dsa_forward_workspace_bytes.argtypes = [i64, i64, i64, i64]
         L.dsa_forward_workspace_bytes.restype = sz
         L.dsa_forward.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
@@ -116,6 +118,11 @@ def sparse_attn(idx, cnt, idx_cap, scores, thr, Q, K, V, O, *, q_row0=0, scale=N
     _check(lib().dsa_sparse_attn(_ptr(idx), _ptr(cnt), idx_cap, _ptr(scores), _ptr(thr), _ptr(Q),
                                  _ptr(K), _ptr(V), _ptr(O), B, T_q, T_k, q_row0, HQ, DQ, DV, scale,
                                  dtype_code(Q), _stream()), "dsa_sparse_attn")
+
+
+def device_status() -> int:
+    """Synchronise the current stream; DSA_OK or DSA_ERR_TIMEOUT (flag read and cleared)."""
+    return int(lib().dsa_device_status(_stream()))
 
 
 def forward_workspace_bytes(B, T_q, T_k, top_k) -> int:

@@ -18,6 +18,7 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
                       int fill_upper, cudaStream_t stream);
 bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype);
+int indexer_tc_take_timeout(cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
                 int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
                 int32_t* idx, int32_t* cnt, int64_t idx_cap, cudaStream_t stream);
@@ -162,6 +163,17 @@ int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, con
     if (!idx) return fail(DSA_ERR_INVALID, "sparse_attn: idx is required (use the threshold form)");
     return sparse_attn(idx, cnt, idx_cap, scores, thr, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ, DV,
                        scale, dtype, (cudaStream_t)stream);
+}
+
+int dsa_device_status(void* stream) {
+    clear_error();
+    const int r = indexer_tc_take_timeout((cudaStream_t)stream);
+    if (r < 0) return fail(DSA_ERR_CUDA, std::string("dsa_device_status: ") +
+                                             cudaGetErrorString(cudaGetLastError()));
+    if (r > 0)
+        return fail(DSA_ERR_TIMEOUT, "a tensor-core indexer launch timed out waiting on its pipeline "
+                                     "(its scores are incomplete)");
+    return DSA_OK;
 }
 
 size_t dsa_forward_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k) {

@@ -20,7 +20,8 @@
 //                 and the tile is stored to the fp32 score matrix
 // Tiles are the causal (query block, key block) pairs, dealt round-robin to
 // the CTAs; all warps walk the same sequence.  Every mbarrier wait is
-// bounded: on timeout the kernel records it in a device flag and leaves.
+// bounded (2 s of device time): on timeout the CTA's warps leave their loops,
+// TMEM is freed, and a device flag records it for dsa_device_status().
 #include <cuda.h>
 #include <math.h>
 #include <stdlib.h>
@@ -50,6 +51,8 @@ struct TcParams {
     int nA, nB;
     uint32_t a_bytes, b_bytes;
     int vec_store;
+    int stall;                  // test hook: the producer issues no loads, so every wait times out
+    unsigned long long timeout_ns;
 };
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -78,14 +81,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait for the phase of parity `parity` to complete.  Gives up after
-// ~2^24 polls (seconds), or as soon as another warp has given up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for the phase of parity `parity` to complete.  Gives up when
+// another warp of the CTA has given up (*abort), or after timeout_ns of
+// device time; then it sets *abort and the sticky device flag that
+// dsa_device_status() reports, and the caller leaves its loop.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
+                                          uint64_t timeout_ns) {
+    uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
         if (mbar_try_wait(b, parity)) return true;
-        if ((i & 1023u) == 1023u) {
-            if (*(volatile int*)&g_indexer_tc_timeout) return false;
-            if (i >= (1u << 24)) {
+        if ((i & 255u) == 255u) {
+            if (*abort) return false;
+            const uint64_t now = global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > timeout_ns) {
+                *abort = 1;
                 atomicExch(&g_indexer_tc_timeout, 1);
                 return false;
             }
@@ -175,6 +190,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ int pref[MAX_TBLK + 1];
     __shared__ uint32_t tmem_slot;
+    __shared__ int s_abort;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -203,6 +219,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         pref[p.n_tblk] = acc;
     }
     if (threadIdx.x == 32) {
+        s_abort = 0;
         for (int s = 0; s < p.nA; ++s) {
             mbar_init(&fullA[s], 1);
             mbar_init(&emptyA[s], 1);
@@ -238,16 +255,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
                 int b, i, j;
                 decode_tile(lin, pref, p, b, i, j);
-                if (!(ok = mbar_wait(&emptyB[bs], bph ^ 1))) break;
-                mbar_expect_tx(&fullB[bs], p.b_bytes);
-                for (int c = 0; c < nch; ++c)
+                if (!(ok = mbar_wait(&emptyB[bs], bph ^ 1, &s_abort, p.timeout_ns))) break;
+                if (!p.stall) mbar_expect_tx(&fullB[bs], p.b_bytes);
+                for (int c = 0; c < nch && !p.stall; ++c)
                     tma_load_3d(sB + (size_t)bs * p.b_bytes + (size_t)c * BN * 128, &tmk, &fullB[bs],
                                 c * KCH, j * BN, b);
                 if (++bs == p.nB) { bs = 0; bph ^= 1; }
                 for (int h = 0; h < p.HI; ++h) {
-                    if (!(ok = mbar_wait(&emptyA[as], aph ^ 1))) break;
-                    mbar_expect_tx(&fullA[as], p.a_bytes);
-                    for (int c = 0; c < nch; ++c)
+                    if (!(ok = mbar_wait(&emptyA[as], aph ^ 1, &s_abort, p.timeout_ns))) break;
+                    if (!p.stall) mbar_expect_tx(&fullA[as], p.a_bytes);
+                    for (int c = 0; c < nch && !p.stall; ++c)
                         tma_load_4d(sA + (size_t)as * p.a_bytes + (size_t)c * BM * 128, &tmq,
                                     &fullA[as], c * KCH, h, i * BM, b);
                     if (++as == p.nA) { as = 0; aph ^= 1; }
@@ -265,11 +282,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t aph = 0, bph = 0, tph = 0;
             bool ok = true;
             for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
-                if (!(ok = mbar_wait(&fullB[bs], bph))) break;
+                if (!(ok = mbar_wait(&fullB[bs], bph, &s_abort, p.timeout_ns))) break;
                 const uint32_t bbase = smem_u32(sB + (size_t)bs * p.b_bytes);
                 for (int h = 0; h < p.HI; ++h) {
-                    if (!(ok = mbar_wait(&fullA[as], aph))) break;
-                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1))) break;
+                    if (!(ok = mbar_wait(&fullA[as], aph, &s_abort, p.timeout_ns))) break;
+                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, &s_abort, p.timeout_ns))) break;
                     tc_fence_after();
                     const uint32_t abase = smem_u32(sA + (size_t)as * p.a_bytes);
                     const uint32_t d = tmem_base + (uint32_t)(tb * BN);
@@ -313,7 +330,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int h = 0; h < p.HI; ++h) {
                 const float wj = wn;
                 if (h + 1 < p.HI) wn = row_ok ? __ldg(wrow + h + 1) : 0.f;
-                if (!(ok = mbar_wait(&tfull[tb], tph))) break;
+                if (!(ok = mbar_wait(&tfull[tb], tph, &s_abort, p.timeout_ns))) break;
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + half * 128);
 #pragma unroll
@@ -372,6 +389,20 @@ __global__ void fill_upper_kernel(float* scores, int64_t T_q, int64_t T_k, int64
 }
 
 }  // namespace
+
+// Synchronises `stream`, reads and clears the timeout flag of this device.
+// Returns 1 if a tensor-core indexer launch gave up on a wait, 0 if not,
+// negative on a CUDA error.
+int indexer_tc_take_timeout(cudaStream_t stream) {
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
+    int flag = 0;
+    if (cudaMemcpyFromSymbol(&flag, g_indexer_tc_timeout, sizeof(int)) != cudaSuccess) return -1;
+    if (flag) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_indexer_tc_timeout, &zero, sizeof(int)) != cudaSuccess) return -1;
+    }
+    return flag ? 1 : 0;
+}
 
 bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype) {
     return dtype == DSA_BF16 && (DI == 64 || DI == 128) && HI >= 1 && HI <= 4096;
@@ -441,6 +472,10 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     p.a_bytes = (uint32_t)(BM * DI * 2);
     p.b_bytes = (uint32_t)(BN * DI * 2);
     p.vec_store = (T_k % 4 == 0) ? 1 : 0;
+    // DSA_TEST_INDEXER_STALL=1: test hook for the timeout path (no loads are
+    // issued, every wait runs out after 20 ms); never set in normal use
+    p.stall = getenv("DSA_TEST_INDEXER_STALL") ? 1 : 0;
+    p.timeout_ns = p.stall ? 20000000ull : 2000000000ull;  // 2 s of device time otherwise
 
     // shared memory: the device's opt-in limit minus the kernel's static
     // shared memory; 1 KB alignment slack + rings + barriers

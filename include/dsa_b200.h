@@ -50,7 +50,8 @@ typedef enum {
     DSA_OK = 0,
     DSA_ERR_INVALID = -1,      /* bad shape, pointer, alignment or argument */
     DSA_ERR_UNSUPPORTED = -2,  /* valid request this build cannot run (e.g. dtype) */
-    DSA_ERR_CUDA = -3          /* a CUDA runtime call failed (launch, attribute) */
+    DSA_ERR_CUDA = -3,         /* a CUDA runtime call failed (launch, attribute) */
+    DSA_ERR_TIMEOUT = -4       /* a kernel gave up waiting on its own pipeline (see dsa_device_status) */
 } dsa_status;
 
 typedef enum { DSA_F32 = 0, DSA_BF16 = 1, DSA_F16 = 2 } dsa_dtype;
@@ -60,6 +61,17 @@ DSA_API int dsa_version(void);
 
 /* Message of the last failing call on this host thread ("" if none). */
 DSA_API const char* dsa_last_error_string(void);
+
+/*
+ * Failure detection.  Every wait inside a kernel (the tensor-core indexer's
+ * mbarrier pipeline) is bounded by 2 s of device time; a kernel that runs out
+ * abandons its work, frees its tensor memory and sets a device flag instead of
+ * hanging.  This call synchronises `stream`, then reads and clears that flag
+ * for the current device: DSA_OK, or DSA_ERR_TIMEOUT if a launch since the
+ * last call gave up (its outputs are incomplete).  No counterpart in the
+ * reference (it has no device-side waits).
+ */
+DSA_API int dsa_device_status(void* stream);
 
 /*
  * Stage 1 — Lightning Indexer scores.
