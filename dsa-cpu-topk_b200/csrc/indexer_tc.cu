@@ -152,20 +152,26 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 columns of this warp's TMEM lane quarter, one 32-bit value per column.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-        "%30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// Wait for this thread's outstanding tcgen05.ld.  The registers of the load
+// whose values are used next are passed through, so no use of them can be
+// scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
 }
 
 // tile index -> (batch, query block, key block) through the per-batch prefix
@@ -333,14 +339,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!(ok = mbar_wait(&tfull[tb], tph, &s_abort, p.timeout_ns))) break;
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + half * 128);
+                // 16-column chunks, the next chunk's load in flight while the
+                // current one is folded in
+                uint32_t rb[2][16];
+                tmem_ld16(taddr, rb[0]);
+                tmem_wait_ld(rb[0]);
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + ch * 32, r);
-                    tmem_wait_ld();
+                for (int ch = 0; ch < 8; ++ch) {
+                    if (ch + 1 < 8) tmem_ld16(taddr + (ch + 1) * 16, rb[(ch + 1) & 1]);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        acc[ch * 32 + e] = fmaf(wj, fmaxf(__uint_as_float(r[e]), 0.f), acc[ch * 32 + e]);
+                    for (int e = 0; e < 16; ++e)
+                        acc[ch * 16 + e] =
+                            fmaf(wj, fmaxf(__uint_as_float(rb[ch & 1][e]), 0.f), acc[ch * 16 + e]);
+                    if (ch + 1 < 8) tmem_wait_ld(rb[(ch + 1) & 1]);
                 }
                 tc_fence_before();
                 __syncwarp();
