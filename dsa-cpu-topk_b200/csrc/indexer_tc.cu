@@ -332,31 +332,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float acc[128];
 #pragma unroll
             for (int c = 0; c < 128; ++c) acc[c] = 0.f;
-            float wn = row_ok ? __ldg(wrow) : 0.f;
-            for (int h = 0; h < p.HI; ++h) {
-                const float wj = wn;
-                if (h + 1 < p.HI) wn = row_ok ? __ldg(wrow + h + 1) : 0.f;
-                if (!(ok = mbar_wait(&tfull[tb], tph, &s_abort, p.timeout_ns))) break;
-                tc_fence_after();
-                const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + half * 128);
-                // 16-column chunks, the next chunk's load in flight while the
-                // current one is folded in
-                uint32_t rb[2][16];
-                tmem_ld16(taddr, rb[0]);
-                tmem_wait_ld(rb[0]);
+            // head weights prefetched two heads ahead (one global-load latency
+            // is about one head's worth of work at DI=64)
+            float wpre[2];
+            wpre[0] = row_ok ? __ldg(wrow) : 0.f;
+            wpre[1] = (row_ok && p.HI > 1) ? __ldg(wrow + 1) : 0.f;
+            for (int h0 = 0; h0 < p.HI && ok; h0 += 2) {
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    if (ch + 1 < 8) tmem_ld16(taddr + (ch + 1) * 16, rb[(ch + 1) & 1]);
+                for (int u = 0; u < 2; ++u) {
+                    const int h = h0 + u;
+                    if (h >= p.HI) break;
+                    const float wj = wpre[u];
+                    wpre[u] = (row_ok && h + 2 < p.HI) ? __ldg(wrow + h + 2) : 0.f;
+                    if (!(ok = mbar_wait(&tfull[tb], tph, &s_abort, p.timeout_ns))) break;
+                    tc_fence_after();
+                    const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + half * 128);
+                    // 16-column chunks, the next chunk's load in flight while the
+                    // current one is folded in
+                    uint32_t rb[2][16];
+                    tmem_ld16(taddr, rb[0]);
+                    tmem_wait_ld(rb[0]);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        acc[ch * 16 + e] =
-                            fmaf(wj, fmaxf(__uint_as_float(rb[ch & 1][e]), 0.f), acc[ch * 16 + e]);
-                    if (ch + 1 < 8) tmem_wait_ld(rb[(ch + 1) & 1]);
+                    for (int ch = 0; ch < 8; ++ch) {
+                        if (ch + 1 < 8) tmem_ld16(taddr + (ch + 1) * 16, rb[(ch + 1) & 1]);
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            acc[ch * 16 + e] =
+                                fmaf(wj, fmaxf(__uint_as_float(rb[ch & 1][e]), 0.f), acc[ch * 16 + e]);
+                        if (ch + 1 < 8) tmem_wait_ld(rb[(ch + 1) & 1]);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[tb]);
+                    if (++tb == 2) { tb = 0; tph ^= 1; }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[tb]);
-                if (++tb == 2) { tb = 0; tph ^= 1; }
             }
             if (!ok || !row_ok) continue;
             const int64_t t = p.q_row0 + tq;
