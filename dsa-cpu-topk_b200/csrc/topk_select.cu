@@ -718,6 +718,169 @@ int launch_warp(const TopkArgs& a, cudaStream_t stream) {
     return check_launch("topk_warp_kernel");
 }
 
+// ===========================================================================
+// Rows of 513..4096 entries: one warp per row, no copy of the row on chip.
+// Every pass re-reads the row (the first read comes from HBM, the rest from
+// L2) so a warp needs only a 512-bin histogram (2 KB); with no block
+// barriers, dozens of rows are in flight per SM, which hides each row's
+// serial chain of sweeps.
+//   passes   9 + 8 + 8 + 7 bits, most significant first; after the first,
+//            only keys matching the selected prefix touch the histogram
+//   emission one more sweep orders the kept positions with ballots
+// ===========================================================================
+constexpr int WL2_BINS = 512;
+
+__device__ __forceinline__ uint4 row_keys4(const float* src, int g, int valid, int vec_ok) {
+    if (vec_ok && 4 * g + 3 < valid) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src) + g);
+        return make_uint4(f2key(v.x), f2key(v.y), f2key(v.z), f2key(v.w));
+    }
+    uint32_t e[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
+    return make_uint4(e[0], e[1], e[2], e[3]);
+}
+
+__global__ void __launch_bounds__(256) topk_warp_l2_kernel(TopkArgs a) {
+    extern __shared__ uint4 wl2_dyn[];  // 8 warps x WL2_BINS
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(wl2_dyn) + warp * WL2_BINS;
+    const uint32_t lt_mask = (1u << lane) - 1u;
+
+    for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.n_rows; row += (int64_t)gridDim.x * 8) {
+        const float* src = a.scores + row * a.row_stride;
+        int valid = (int)a.row_len;
+        if (a.causal) {
+            const int64_t t = a.q_row0 + row % a.rows_per_batch;
+            valid = t + 1 < a.row_len ? (int)(t + 1) : (int)a.row_len;
+        }
+        if (a.k > valid) {
+            if (lane == 0) {
+                a.thr[row] = __uint_as_float(0xff800000u);
+                if (a.cnt) a.cnt[row] = valid;
+            }
+            if (a.idx) {
+                const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
+                for (int i = lane; i < n; i += 32) a.idx[row * a.idx_cap + i] = i;
+            }
+            continue;
+        }
+        const int g4 = (valid + 3) >> 2;
+        uint32_t prefix = 0, pmask = 0, krem = (uint32_t)a.k, bin_n = 0;
+#pragma unroll 1
+        for (int pass = 0; pass < 4; ++pass) {
+            const int bits = pass == 0 ? 9 : pass == 3 ? 7 : 8;
+            const int shift = pass == 0 ? 23 : pass == 1 ? 15 : pass == 2 ? 7 : 0;
+            const uint32_t nb = 1u << bits;
+            // clear this warp's slots
+#pragma unroll
+            for (int q = 0; q < WL2_BINS / 128; ++q) reinterpret_cast<uint4*>(hist)[lane + 32 * q] = make_uint4(0, 0, 0, 0);
+            __syncwarp();
+            // slot = WL2_BINS - 1 - digit (descending digits)
+            for (int g0 = lane; g0 < g4; g0 += 32 * 4) {
+                uint4 kk[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int g = g0 + 32 * u;
+                    kk[u] = g < g4 ? row_keys4(src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int g = g0 + 32 * u;
+                    const uint32_t e[4] = {kk[u].x, kk[u].y, kk[u].z, kk[u].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (4 * g + j < valid && (e[j] & pmask) == prefix)
+                            atomicAdd(&hist[(WL2_BINS - 1) - ((e[j] >> shift) & (nb - 1))], 1u);
+                }
+            }
+            __syncwarp();
+            // warp scan: lane owns slots [SPL*lane, SPL*lane+SPL)
+            constexpr int SPL = WL2_BINS / 32;
+            uint32_t local = 0;
+#pragma unroll
+            for (int q = 0; q < SPL / 4; ++q) {
+                const uint4 h = reinterpret_cast<const uint4*>(hist)[lane * (SPL / 4) + q];
+                local += h.x + h.y + h.z + h.w;
+            }
+            uint32_t incl = local;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t excl = incl - local;
+            const bool mine = excl < krem && krem <= incl;
+            uint32_t dig = 0, kr = 0, bn = 0;
+            if (mine) {
+                uint32_t c = excl;
+                for (int q = 0; q < SPL; ++q) {
+                    const uint32_t h = hist[lane * SPL + q];
+                    if (krem <= c + h) {
+                        dig = (uint32_t)(WL2_BINS - (lane * SPL + q));  // digit + 1
+                        kr = krem - c;
+                        bn = h;
+                        break;
+                    }
+                    c += h;
+                }
+            }
+            const uint32_t who = __ballot_sync(0xffffffffu, mine);
+            const int srcl = who ? __ffs(who) - 1 : 0;
+            dig = __shfl_sync(0xffffffffu, dig, srcl);
+            kr = __shfl_sync(0xffffffffu, kr, srcl);
+            bin_n = __shfl_sync(0xffffffffu, bn, srcl);
+            prefix |= (dig - 1u) << shift;
+            pmask |= (nb - 1) << shift;
+            krem = kr;
+            __syncwarp();
+        }
+        const uint32_t thr_key = prefix;
+        // kept = keys above the k-th (k - krem of them) + keys equal to it (the final bin)
+        const uint32_t total = (uint32_t)a.k - krem + bin_n;
+        if (lane == 0) {
+            a.thr[row] = key2f(thr_key);
+            if (a.cnt) a.cnt[row] = (int32_t)total;
+        }
+        if (a.idx) {
+            int32_t* out = a.idx + row * a.idx_cap;
+            const uint32_t cap = (uint32_t)a.idx_cap;
+            uint32_t base = 0;
+            for (int gb = 0; gb < g4 && base < cap; gb += 32) {
+                const int g = gb + lane;
+                const uint4 kk = g < g4 ? row_keys4(src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
+                const bool p0 = 4 * g < valid && kk.x >= thr_key, p1 = 4 * g + 1 < valid && kk.y >= thr_key,
+                           p2 = 4 * g + 2 < valid && kk.z >= thr_key, p3 = 4 * g + 3 < valid && kk.w >= thr_key;
+                const uint32_t m0 = __ballot_sync(0xffffffffu, p0), m1 = __ballot_sync(0xffffffffu, p1),
+                               m2 = __ballot_sync(0xffffffffu, p2), m3 = __ballot_sync(0xffffffffu, p3);
+                uint32_t pos = base + __popc(m0 & lt_mask) + __popc(m1 & lt_mask) + __popc(m2 & lt_mask) +
+                               __popc(m3 & lt_mask);
+                if (p0) { if (pos < cap) out[pos] = 4 * g; ++pos; }
+                if (p1) { if (pos < cap) out[pos] = 4 * g + 1; ++pos; }
+                if (p2) { if (pos < cap) out[pos] = 4 * g + 2; ++pos; }
+                if (p3) { if (pos < cap) out[pos] = 4 * g + 3; ++pos; }
+                base += __popc(m0) + __popc(m1) + __popc(m2) + __popc(m3);
+            }
+        }
+    }
+}
+
+int launch_warp_l2(const TopkArgs& a, cudaStream_t stream) {
+    const size_t smem = 8 * WL2_BINS * sizeof(uint32_t);
+    if (cudaFuncSetAttribute(topk_warp_l2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return fail(DSA_ERR_CUDA, "topk_select: cannot set dynamic shared memory size");
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, topk_warp_l2_kernel, 256, smem) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    int64_t grid = (int64_t)num_sms() * per_sm;
+    const int64_t need = (a.n_rows + 7) / 8;
+    if (grid > need) grid = need;
+    topk_warp_l2_kernel<<<(unsigned)grid, 256, smem, stream>>>(a);
+    return check_launch("topk_warp_l2_kernel");
+}
+
 }  // namespace
 
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
@@ -764,6 +927,10 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
         if (longest <= 256) return launch_warp<2, 256>(a, stream);
         return launch_warp<4, 256>(a, stream);
     }
+    // rows of 513..4096: one warp per row re-reading the row from L2 (measured
+    // faster than a CTA per row there; slower on the long rows of c4/c5)
+    if (longest <= 4096 && !getenv("DSA_TOPK_LONG_PATH") && !getenv("DSA_TOPK_NO_WL2"))
+        return launch_warp_l2(a, stream);
     if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
         if (longest <= 2048) return launch_cached<128, true>(a, longest, stream);
         if (longest <= 8192) return launch_cached<256, true>(a, longest, stream);

@@ -145,3 +145,16 @@ def test_block_kernel_on_short_rows_exact(cuda, N, k, monkeypatch):
     assert_same(x, k)
     s = torch.randn(3, 64, N, generator=g)
     assert_same(s, min(k, N), causal=True, q_row0=max(0, N - 70))
+
+
+@pytest.mark.parametrize("N,k", [(600, 32), (2048, 128), (4096, 512)])
+def test_cta_kernel_on_mid_rows_exact(cuda, N, k, monkeypatch):
+    """Rows of 513..4096 normally run one warp per row; the CTA-per-row
+    kernel, forced on them, gives the same exact result."""
+    monkeypatch.setenv("DSA_TOPK_NO_WL2", "1")
+    g = torch.Generator().manual_seed(N + 5 * k)
+    x = torch.randn(20, N, generator=g)
+    x[2] = torch.round(x[2] * 2)
+    assert_same(x, k)
+    s = torch.randn(2, 30, N, generator=g)
+    assert_same(s, k, causal=True, q_row0=N - 25)
