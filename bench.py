@@ -46,8 +46,11 @@ CONFIGS = {
                desc="DSA fwd B4 T8192 k512 HI16 DI64 HQ16 D64 bf16, causal"),
     "c5": dict(B=1, T=32768, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16",
                desc="DSA fwd B1 T32768 k2048 HI64 DI128 HQ16 D128 bf16, causal (DeepSeek-V3.2 scale)"),
+    # c5 with the indexer inputs in FP8 (e4m3) as in the DeepSeek-V3.2 paper; not a BASELINE config
+    "c5_fp8": dict(B=1, T=32768, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16", idx_dtype="fp8",
+                   desc="c5 with e4m3 indexer q/k (FP8 indexer), bf16 Q/K/V"),
 }
-DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+DT = {"f32": torch.float32, "bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}
 C2 = dict(B=64, T=2048, k=128, desc="top-K only: fp32 scores 64 x 2048 x 2048, N(0,1), s > t = -inf, k=128")
 
 
@@ -135,7 +138,8 @@ def make_inputs_device(cfg, B, dev, seed):
     def rnd(shape, scale=1.0, dtype=dt):
         return (torch.randn(shape, generator=g, device=dev) * scale).to(dtype)
 
-    return (rnd((B, T, HI, DI)), rnd((B, T, DI)), rnd((B, T, HI), 1 / math.sqrt(HI), torch.float32),
+    it = DT[cfg.get("idx_dtype", cfg["dtype"])]
+    return (rnd((B, T, HI, DI), dtype=it), rnd((B, T, DI), dtype=it), rnd((B, T, HI), 1 / math.sqrt(HI), torch.float32),
             rnd((B, T, HQ, D)), rnd((B, T, HQ, D)), rnd((B, T, HQ, D)))
 
 
@@ -402,8 +406,10 @@ def run_b200(args, cfg, world, rank, local):
     traffic = load_traffic().get(args.config, {})
     stages = {
         "indexer": dict(bound="tensor", achieved=alg["indexer_flops"] / (stage_ms[0] / 1e3) / 1e12,
-                        peak=tf_sust, unit="TFLOP/s", ms=stage_ms[0],
-                        kernel="indexer_tc" if cfg["dtype"] == "bf16" else "indexer_simt (fp32 CUDA cores)",
+                        peak=tf_sust * (2 if cfg.get("idx_dtype") == "fp8" else 1), unit="TFLOP/s",
+                        ms=stage_ms[0],
+                        kernel=("indexer_tc (e4m3, kind::f8f6f4)" if cfg.get("idx_dtype") == "fp8" else
+                                "indexer_tc" if cfg["dtype"] == "bf16" else "indexer_simt (fp32 CUDA cores)"),
                         traffic=traffic.get("indexer")),
         "topk": dict(bound="hbm", achieved=alg["topk_bytes"] / (stage_ms[1] / 1e3) / 1e9, peak=hbm,
                      unit="GB/s", ms=stage_ms[1], kernel="topk_select_kernel", traffic=traffic.get("topk")),
@@ -414,6 +420,8 @@ def run_b200(args, cfg, world, rank, local):
     for v in stages.values():
         v["frac"] = v["achieved"] / v["peak"]
         v["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
+    if cfg.get("idx_dtype") == "fp8":
+        stages["indexer"]["peak_source"] += "; FP8 peak taken as 2x the measured sustained bf16 (none measured)"
     if pipe.fused:
         elt = 2 if cfg["dtype"] == "bf16" else 4
         io = sum(x.numel() * x.element_size() for x in inputs[:4]) + B * T * cfg["HQ"] * cfg["D"] * 4

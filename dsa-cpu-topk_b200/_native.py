@@ -17,8 +17,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdsa_b200.so")
 
 DSA_OK, DSA_ERR_INVALID, DSA_ERR_UNSUPPORTED, DSA_ERR_CUDA, DSA_ERR_TIMEOUT = 0, -1, -2, -3, -4
-DSA_F32, DSA_BF16, DSA_F16 = 0, 1, 2
-_DTYPES = {torch.float32: DSA_F32, torch.bfloat16: DSA_BF16, torch.float16: DSA_F16}
+DSA_F32, DSA_BF16, DSA_F16, DSA_FP8_E4M3 = 0, 1, 2, 3
+_DTYPES = {torch.float32: DSA_F32, torch.bfloat16: DSA_BF16, torch.float16: DSA_F16,
+           torch.float8_e4m3fn: DSA_FP8_E4M3}
 
 _lib = None
 
@@ -67,7 +68,7 @@ def dtype_code(t: torch.Tensor) -> int:
     try:
         return _DTYPES[t.dtype]
     except KeyError:
-        raise AssertionError(f"unsupported dtype {t.dtype} (fp32, bf16, fp16)") from None
+        raise AssertionError(f"unsupported dtype {t.dtype} (fp32, bf16, fp16; e4m3 for indexer inputs)") from None
 
 
 def prep(t: torch.Tensor) -> torch.Tensor:

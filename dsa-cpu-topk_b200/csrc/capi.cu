@@ -16,7 +16,7 @@ int indexer_scores_simt(const void* q, const void* k, const float* w, float* sco
                         int dtype, int fill_upper, cudaStream_t stream);
 int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                      int fill_upper, cudaStream_t stream);
+                      int fill_upper, int dtype, cudaStream_t stream);
 bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype);
 int indexer_tc_take_timeout(cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
@@ -110,7 +110,7 @@ static int run_indexer(const void* q, const void* k, const float* w, float* scor
                        int fill_upper, cudaStream_t st) {
     if (indexer_tc_supported(HI, DI, dtype) && aligned16(q) && aligned16(k) && aligned16(scores) &&
         aligned16(w) && !force_simt()) {
-        const int rc = indexer_scores_tc(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, st);
+        const int rc = indexer_scores_tc(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, dtype, st);
         if (rc != -100) return rc;  // -100: shape beyond the tensor-core kernel's limits
     }
     return indexer_scores_simt(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper, st);

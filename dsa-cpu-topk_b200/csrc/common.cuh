@@ -4,6 +4,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -21,8 +22,11 @@ int check_launch(const char* what);
 int num_sms();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-inline size_t dtype_size(int dt) { return dt == DSA_F32 ? 4 : 2; }
-inline bool dtype_ok(int dt) { return dt == DSA_F32 || dt == DSA_BF16 || dt == DSA_F16; }
+inline size_t dtype_size(int dt) { return dt == DSA_F32 ? 4 : dt == DSA_FP8_E4M3 ? 1 : 2; }
+// dtypes of the indexer inputs (q, k); the attention inputs exclude FP8
+inline bool dtype_ok(int dt) {
+    return dt == DSA_F32 || dt == DSA_BF16 || dt == DSA_F16 || dt == DSA_FP8_E4M3;
+}
 
 // ---- device helpers --------------------------------------------------------
 template <typename T> struct Elem;
@@ -34,6 +38,9 @@ template <> struct Elem<__nv_bfloat16> {
 };
 template <> struct Elem<__half> {
     static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+};
+template <> struct Elem<__nv_fp8_e4m3> {
+    static __device__ __forceinline__ float to_f(__nv_fp8_e4m3 x) { return float(x); }
 };
 
 // 16 bytes of T -> 16/sizeof(T) floats.

@@ -280,6 +280,9 @@ int indexer_scores_simt(const void* q, const void* k, const float* w, float* sco
         case DSA_BF16:
             return launch<__nv_bfloat16>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper,
                                          stream);
+        case DSA_FP8_E4M3:
+            return launch<__nv_fp8_e4m3>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper,
+                                         stream);
         default:
             return launch<__half>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, stream);
     }

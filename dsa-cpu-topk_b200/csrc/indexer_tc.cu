@@ -1,11 +1,15 @@
-// Stage 1 (tensor-core path): tcgen05 / TMEM Lightning Indexer for bf16 inputs.
+// Stage 1 (tensor-core path): tcgen05 / TMEM Lightning Indexer for bf16 or
+// FP8 (e4m3) inputs.
 //
 //   I[b,t,s] = sum_j w[b,t,j] * ReLU(<q[b,t,j,:], k[b,s,:]>),  s <= t
 //
 // The reference computes this with an IEEE-fp32 tl.dot per head on CUDA
 // cores (lightning_indexer.py:83-90).  Here each head's dot products are one
-// bf16 GEMM on the 5th-generation tensor cores with fp32 accumulation in
+// bf16 (kind::f16) or e4m3 (kind::f8f6f4, the FP8 indexer of the DeepSeek-V3.2
+// paper) GEMM on the 5th-generation tensor cores with fp32 accumulation in
 // tensor memory, and the ReLU * w[t,j] head reduction runs in the epilogue.
+// Products of e4m3 (or bf16) values are exact in fp32, so both are faithful
+// to the reference's fp32 arithmetic on the same inputs.
 //
 // Persistent, warp-specialised, one CTA per SM:
 //   warp 0        TMA producer: per tile one key block k[s0:s0+256, :] (B operand),
@@ -36,7 +40,7 @@ namespace {
 
 constexpr int BM = 128;            // query rows per tile (TMEM lanes)
 constexpr int BN = 256;            // keys per tile (MMA N, TMEM columns per accumulator)
-constexpr int KCH = 64;            // bf16 elements per 128-byte swizzle row
+constexpr int ROWB = 128;          // bytes per swizzle row (one K chunk): 64 bf16 or 128 e4m3
 constexpr int EPI_WARPS = 8;
 constexpr int NTHREADS = 64 + EPI_WARPS * 32;
 constexpr int MAX_TBLK = 1024;     // query blocks per batch (T_q <= 131072)
@@ -51,6 +55,7 @@ struct TcParams {
     int nA, nB;
     uint32_t a_bytes, b_bytes;
     int vec_store;
+    int elt;                    // bytes per q/k element: 2 (bf16) or 1 (e4m3)
     int stall;                  // test hook: the producer issues no loads, so every wait times out
     unsigned long long timeout_ns;
 };
@@ -133,13 +138,24 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     d |= (uint64_t)2 << 61;             // SWIZZLE_128B
     return d;
 }
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+// D (TMEM, fp32) (+)= A * B^T for one 32-byte K slice: bf16 (kind::f16,
+// K=16) or e4m3 (kind::f8f6f4, K=32)
+template <bool FP8>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t accumulate) {
+    if constexpr (FP8) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    }
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -190,6 +206,7 @@ __device__ __forceinline__ void decode_tile(int lin, const int* pref, const TcPa
     j = r - pref[lo];
 }
 
+template <bool FP8>
 __global__ void __launch_bounds__(NTHREADS, 1)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                       const TcParams p) {
@@ -209,7 +226,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t* tempty = tfull + 2;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nch = p.DI / KCH;
+    const int nch = p.DI * p.elt / ROWB;   // 128-byte K chunks per row
+    const int kch = ROWB / p.elt;          // elements per chunk (TMA x step)
 
     if (threadIdx.x == 0) {
         int acc = 0;
@@ -265,14 +283,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!p.stall) mbar_expect_tx(&fullB[bs], p.b_bytes);
                 for (int c = 0; c < nch && !p.stall; ++c)
                     tma_load_3d(sB + (size_t)bs * p.b_bytes + (size_t)c * BN * 128, &tmk, &fullB[bs],
-                                c * KCH, j * BN, b);
+                                c * kch, j * BN, b);
                 if (++bs == p.nB) { bs = 0; bph ^= 1; }
                 for (int h = 0; h < p.HI; ++h) {
                     if (!(ok = mbar_wait(&emptyA[as], aph ^ 1, &s_abort, p.timeout_ns))) break;
                     if (!p.stall) mbar_expect_tx(&fullA[as], p.a_bytes);
                     for (int c = 0; c < nch && !p.stall; ++c)
                         tma_load_4d(sA + (size_t)as * p.a_bytes + (size_t)c * BM * 128, &tmq,
-                                    &fullA[as], c * KCH, h, i * BM, b);
+                                    &fullA[as], c * kch, h, i * BM, b);
                     if (++as == p.nA) { as = 0; aph ^= 1; }
                 }
             }
@@ -280,9 +298,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            // kind::f16: D fp32 (bit 4), A bf16 (bits 7-9), B bf16 (bits 10-12),
-            // both K-major, N>>3 at bit 17, M>>4 at bit 24
-            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+            // D fp32 (bit 4); A/B formats at bits 7-9 / 10-12 (kind::f16: 1 = bf16;
+            // kind::f8f6f4: 0 = e4m3); both K-major, N>>3 at bit 17, M>>4 at bit 24
+            const uint32_t fmt = FP8 ? 0u : 1u;
+            const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                                    ((uint32_t)(BM >> 4) << 24);
             int as = 0, bs = 0, tb = 0;
             uint32_t aph = 0, bph = 0, tph = 0;
@@ -298,10 +317,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const uint32_t d = tmem_base + (uint32_t)(tb * BN);
                     for (int c = 0; c < nch; ++c) {
 #pragma unroll
-                        for (int kk = 0; kk < KCH / 16; ++kk) {
+                        for (int kk = 0; kk < ROWB / 32; ++kk) {
                             const uint64_t ad = sw128_desc(abase + c * BM * 128 + kk * 32);
                             const uint64_t bd = sw128_desc(bbase + c * BN * 128 + kk * 32);
-                            umma_bf16(d, ad, bd, idesc, (c | kk) != 0);
+                            umma<FP8>(d, ad, bd, idesc, (c | kk) != 0);
                         }
                     }
                     umma_commit(&emptyA[as]);
@@ -425,7 +444,10 @@ int indexer_tc_take_timeout(cudaStream_t stream) {
 }
 
 bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype) {
-    return dtype == DSA_BF16 && (DI == 64 || DI == 128) && HI >= 1 && HI <= 4096;
+    if (HI < 1 || HI > 4096) return false;
+    if (dtype == DSA_BF16) return DI == 64 || DI == 128;
+    if (dtype == DSA_FP8_E4M3) return DI == 128 || DI == 256;
+    return false;
 }
 
 // cuTensorMapEncodeTiled is looked up through the runtime, so the library
@@ -449,12 +471,12 @@ static EncodeTiledFn encode_fn() {
 }
 
 static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
-                      const cuuint64_t* strides, const cuuint32_t* box, const char* what) {
+                      const cuuint64_t* strides, const cuuint32_t* box, const char* what, int elt) {
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(DSA_ERR_CUDA, "indexer_tc: cuTensorMapEncodeTiled not available");
     const CUresult r = enc(
-        m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
+        m, elt == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
@@ -465,8 +487,11 @@ static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64
 
 int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                      int fill_upper, cudaStream_t stream) {
+                      int fill_upper, int dtype, cudaStream_t stream) {
     TcParams p;
+    p.elt = dtype == DSA_FP8_E4M3 ? 1 : 2;
+    const bool fp8 = p.elt == 1;
+    auto kern = fp8 ? indexer_tc_kernel<true> : indexer_tc_kernel<false>;
     p.scores = scores;
     p.w = w;
     p.T_q = T_q;
@@ -489,8 +514,8 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     if (per_batch * B > INT32_MAX) return -100;
     p.tiles_per_batch = (int)per_batch;
     p.total_tiles = (int)(per_batch * B);
-    p.a_bytes = (uint32_t)(BM * DI * 2);
-    p.b_bytes = (uint32_t)(BN * DI * 2);
+    p.a_bytes = (uint32_t)(BM * DI * p.elt);
+    p.b_bytes = (uint32_t)(BN * DI * p.elt);
     p.vec_store = (T_k % 4 == 0) ? 1 : 0;
     // DSA_TEST_INDEXER_STALL=1: test hook for the timeout path (no loads are
     // issued, every wait runs out after 20 ms); never set in normal use
@@ -503,7 +528,7 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     cudaFuncAttributes fa;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncGetAttributes(&fa, indexer_tc_kernel) != cudaSuccess)
+        cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
         return fail(DSA_ERR_CUDA, "indexer_tc: cannot query shared memory limits");
     const size_t kMaxSmem = (size_t)optin - fa.sharedSizeBytes;
     const size_t fixed = 1024 + 256;
@@ -525,25 +550,25 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     CUtensorMap tmq, tmk;
     {
         const cuuint64_t dims[4] = {(cuuint64_t)DI, (cuuint64_t)HI, (cuuint64_t)T_q, (cuuint64_t)B};
-        const cuuint64_t str[3] = {(cuuint64_t)DI * 2, (cuuint64_t)HI * DI * 2,
-                                   (cuuint64_t)T_q * HI * DI * 2};
-        const cuuint32_t box[4] = {KCH, 1, BM, 1};
-        int rc = encode_map(&tmq, q, 4, dims, str, box, "q");
+        const cuuint64_t e = (cuuint64_t)p.elt;
+        const cuuint64_t str[3] = {(cuuint64_t)DI * e, (cuuint64_t)HI * DI * e, (cuuint64_t)T_q * HI * DI * e};
+        const cuuint32_t box[4] = {(cuuint32_t)(ROWB / p.elt), 1, BM, 1};
+        int rc = encode_map(&tmq, q, 4, dims, str, box, "q", p.elt);
         if (rc) return rc;
     }
     {
         const cuuint64_t dims[3] = {(cuuint64_t)DI, (cuuint64_t)T_k, (cuuint64_t)B};
-        const cuuint64_t str[2] = {(cuuint64_t)DI * 2, (cuuint64_t)T_k * DI * 2};
-        const cuuint32_t box[3] = {KCH, BN, 1};
-        int rc = encode_map(&tmk, k, 3, dims, str, box, "k");
+        const cuuint64_t e = (cuuint64_t)p.elt;
+        const cuuint64_t str[2] = {(cuuint64_t)DI * e, (cuuint64_t)T_k * DI * e};
+        const cuuint32_t box[3] = {(cuuint32_t)(ROWB / p.elt), BN, 1};
+        int rc = encode_map(&tmk, k, 3, dims, str, box, "k", p.elt);
         if (rc) return rc;
     }
-    if (cudaFuncSetAttribute(indexer_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return fail(DSA_ERR_CUDA, "indexer_tc: cannot set dynamic shared memory size");
     int grid = num_sms();
     if (grid > p.total_tiles) grid = p.total_tiles;
-    indexer_tc_kernel<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, p);
+    kern<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, p);
     return check_launch("indexer_tc_kernel");
 }
 

@@ -496,6 +496,8 @@ int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const f
     if (B < 0 || T_q < 0 || T_k < 1 || q_row0 < 0 || HQ < 1 || DQ < 1 || DV < 1)
         return fail(DSA_ERR_INVALID, "sparse_attn: bad sizes");
     if (!dtype_ok(dtype)) return fail(DSA_ERR_INVALID, "sparse_attn: unknown dtype");
+    if (dtype == DSA_FP8_E4M3)
+        return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: FP8 is supported for the indexer inputs only");
     if (DQ != DV)
         return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: DQ != DV is not supported by this build");
     if (!Q || !K || !V || !O) return fail(DSA_ERR_INVALID, "sparse_attn: null Q/K/V/O");

@@ -54,7 +54,8 @@ typedef enum {
     DSA_ERR_TIMEOUT = -4       /* a kernel gave up waiting on its own pipeline (see dsa_device_status) */
 } dsa_status;
 
-typedef enum { DSA_F32 = 0, DSA_BF16 = 1, DSA_F16 = 2 } dsa_dtype;
+/* DSA_FP8_E4M3 is accepted for the indexer inputs (q, k) only. */
+typedef enum { DSA_F32 = 0, DSA_BF16 = 1, DSA_F16 = 2, DSA_FP8_E4M3 = 3 } dsa_dtype;
 
 /* Library version, (major << 16) | minor. */
 DSA_API int dsa_version(void);
@@ -81,8 +82,9 @@ DSA_API int dsa_device_status(void* stream);
  *   scores  [B, T_q, T_k]     fp32 out   score of causal entries; entries s > t are
  *                                        written -inf when fill_upper != 0, else left
  *                                        untouched or -inf (stages 2/3 never read them)
- * dtype DSA_BF16 with DI % 16 == 0 runs on the tcgen05 tensor cores; other
- * shapes and DSA_F32 run the fp32 CUDA-core kernel (IEEE fp32 products and sums).
+ * dtype DSA_BF16 with DI in {64, 128} and DSA_FP8_E4M3 with DI in {128, 256}
+ * run on the tcgen05 tensor cores; other shapes and dtypes run the fp32
+ * CUDA-core kernel (IEEE fp32 products and sums).
  * Replaces lightning_indexer.py:100-125 (which requires DI a power of two).
  */
 DSA_API int dsa_indexer_scores(const void* q, const void* k, const float* w, float* scores,

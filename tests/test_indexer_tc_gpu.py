@@ -72,3 +72,47 @@ def test_tc_fill_upper_contract(cuda):
     assert torch.isneginf(full[0][upper]).all()
     part = scores(q, k, w, fill_upper=False)
     assert torch.equal(part[0][~upper], full[0][~upper])
+
+
+@pytest.mark.parametrize("B,T_q,T_k,q0,HI,DI", [
+    (1, 300, 300, 0, 4, 128),
+    (2, 700, 700, 0, 8, 128),
+    (1, 129, 1001, 872, 2, 256),
+    (1, 2048, 2048, 0, 64, 128),     # c5 head shapes
+])
+def test_fp8_tc_matches_simt_and_oracle(cuda, B, T_q, T_k, q0, HI, DI):
+    """FP8 (e4m3) indexer inputs on the tensor cores (kind::f8f6f4).  Products
+    of e4m3 values are exact in fp32, so the scores match the fp32 oracle on
+    the upcast inputs to fp32 rounding."""
+    g = torch.Generator().manual_seed(T_q + HI)
+    q8 = (torch.randn(B, T_q, HI, DI, generator=g) * 2).to(torch.float8_e4m3fn)
+    k8 = (torch.randn(B, T_k, DI, generator=g) * 2).to(torch.float8_e4m3fn)
+    w = torch.randn(B, T_q, HI, generator=g) / HI ** 0.5
+    dq, dk, dw = q8.to(cuda), k8.to(cuda), w.to(cuda)
+    tc = scores(dq, dk, dw, q_row0=q0).cpu()
+    sm = simt_scores(dq, dk, dw, q_row0=q0).cpu()
+    fin = torch.isfinite(sm)
+    assert torch.equal(torch.isfinite(tc), fin)
+    qf, kf = q8.float(), k8.float()
+    scale = torch.einsum("bthd,bsd->bts", qf.abs(), kf.abs()).mean().item()
+    assert (tc[fin] - sm[fin]).abs().max().item() < 1e-5 * scale * HI ** 0.5 + 1e-6
+    qfull = torch.zeros(B, q0 + T_q, HI, DI)
+    wfull = torch.zeros(B, q0 + T_q, HI)
+    qfull[:, q0:], wfull[:, q0:] = qf, w
+    if kf.shape[1] < qfull.shape[1]:
+        kf = torch.cat([kf, torch.zeros(B, qfull.shape[1] - kf.shape[1], DI)], 1)
+    ref = o.indexer_scores(qfull, kf, wfull, slice(q0, q0 + T_q), T_k=T_k)
+    assert bool(((tc[fin] - ref[fin]).abs() <= 1e-3 * ref[fin].abs() + 1e-5 * scale).all())
+
+
+def test_fp8_indexer_in_forward(cuda):
+    """Forward with FP8 indexer inputs and bf16 attention inputs, against the
+    oracle run on the upcast values."""
+    from dsa_attention import dsa_forward
+    B, T, HI, DI, HQ, D, k = 1, 1024, 8, 128, 4, 64, 64
+    qi, ki, wi, Q, K, V = o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=torch.bfloat16)
+    qi8, ki8 = qi.float().to(torch.float8_e4m3fn), ki.float().to(torch.float8_e4m3fn)
+    out = dsa_forward(qi8.to(cuda), ki8.to(cuda), wi.to(cuda), Q.to(cuda), K.to(cuda), V.to(cuda), k).cpu()
+    ref = o.dsa_attention(qi8.float(), ki8.float(), wi, Q, K, V, k)
+    bad = ((out - ref).abs() > 2e-2 * ref.abs() + 2e-2).any(-1).any(-1)
+    assert bad.float().mean() < 0.002
