@@ -168,7 +168,15 @@ class Pipeline:
                      idx=torch.empty((B * Tq, self.cap), device=dev, dtype=torch.int32),
                      O=torch.empty((B, Tq, Q.shape[2], V.shape[3]), device=dev, dtype=torch.float32))
             self.parts.append(p)
-        self.launches_per_step = 3 * len(self.parts)
+        # stage 3 on the tensor cores (kept-set bitmap + masked flash attention)
+        # where the dtype and head size allow, else the gather over kept lists
+        self.tc = _native.attn_tc_supported(Q, V) and os.environ.get("DSA_ATTN_GATHER") != "1"
+        self.words = _native.bitmap_words(T)
+        if self.tc:
+            for p in self.parts:
+                p["bits"] = torch.empty((B * p["Tq"], self.words), device=dev, dtype=torch.int32)
+        self.stage_names = ["indexer", "topk", "sparse_attn"]
+        self.launches_per_step = len(self.stage_names) * len(self.parts)
         # opt-in one-launch kernel for short sequences (DSA_FUSED_SMALL=1)
         self.fused = T <= 512 and bool(os.environ.get("DSA_FUSED_SMALL"))
         if self.fused:
@@ -178,43 +186,46 @@ class Pipeline:
             self.ws = [torch.empty(forward_workspace_bytes(B, p["Tq"], T, self.k), device=dev, dtype=torch.uint8)
                        for p in self.parts]
             self.launches_per_step = len(self.parts)
-            self.step_staged(None)  # untimed: fills the kept counts used for accounting
+            self.stage_names = ["fused_forward"]
+        self.step(None)  # untimed: fills the kept counts used for accounting
+        for p in self.parts:
+            B, Tq, T = p["scores"].shape
+            if self.tc or self.fused:
+                self.n.topk_select(p["scores"], B * Tq, T, T, self.k, p["thr"], None, p["cnt"], 0,
+                                   causal=True, rows_per_batch=Tq, q_row0=p["q0"])
 
     def step(self, ev=None):
-        if not self.fused:
-            return self.step_staged(ev)
-        for i, p in enumerate(self.parts):
-            if ev is not None:
-                ev[i][0].record()
-            self.n.forward(p["q"], self.k_idx, p["w"], p["Q"], self.K, self.V, p["O"], self.k, self.ws[i],
-                           q_row0=p["q0"])
-            if ev is not None:
-                for j in (1, 2, 3):
-                    ev[i][j].record()
-
-    def step_staged(self, ev=None):
+        """One forward over every row block; ev[i][j] brackets stage j of block i."""
         n = self.n
         for i, p in enumerate(self.parts):
-            if ev is not None:
-                ev[i][0].record()
+            rec = (lambda j: ev[i][j].record()) if ev is not None else (lambda j: None)
+            rec(0)
+            if self.fused:
+                n.forward(p["q"], self.k_idx, p["w"], p["Q"], self.K, self.V, p["O"], self.k, self.ws[i],
+                          q_row0=p["q0"])
+                rec(1)
+                continue
             n.indexer_scores(p["q"], self.k_idx, p["w"], p["scores"], q_row0=p["q0"], fill_upper=False)
-            if ev is not None:
-                ev[i][1].record()
+            rec(1)
             B, Tq, T = p["scores"].shape
+            if self.tc:
+                n.topk_select_bitmap(p["scores"], self.k, p["thr"], p["bits"], causal=True, q_row0=p["q0"])
+                rec(2)
+                n.sparse_attn_bitmap(p["bits"], p["Q"], self.K, self.V, p["O"], q_row0=p["q0"])
+                rec(3)
+                continue
             n.topk_select(p["scores"], B * Tq, T, T, self.k, p["thr"], p["idx"], p["cnt"], self.cap,
                           causal=True, rows_per_batch=Tq, q_row0=p["q0"])
-            if ev is not None:
-                ev[i][2].record()
+            rec(2)
             n.sparse_attn(p["idx"], p["cnt"], self.cap, p["scores"], p["thr"], p["Q"], self.K, self.V,
                           p["O"], q_row0=p["q0"])
-            if ev is not None:
-                ev[i][3].record()
+            rec(3)
 
     def algorithmic(self, cfg):
         """Per-step algorithmic work of each stage (from the actual kept counts)."""
         elt = 2 if cfg["dtype"] == "bf16" else 4
         HI, DI, HQ, D = cfg["HI"], cfg["DI"], cfg["HQ"], cfg["D"]
-        flops = topk_b = attn_b = attn_f = 0
+        flops = topk_b = attn_b = attn_f = tile_f = 0
         for p in self.parts:
             B, Tq, T = p["scores"].shape
             t = torch.arange(p["q0"], p["q0"] + Tq, dtype=torch.float64)
@@ -222,10 +233,18 @@ class Pipeline:
             sel = p["cnt"].double().sum().item()
             rows = B * Tq
             flops += 2.0 * HI * DI * valid
-            topk_b += 4.0 * valid + 8.0 * rows + 4.0 * sel
+            topk_b += 4.0 * valid + (4.0 * rows + 4.0 * rows * self.words if self.tc
+                                     else 8.0 * rows + 4.0 * sel)
             attn_b += sel * HQ * 2 * D * elt + rows * HQ * D * (elt + 4) + 4.0 * sel + 4.0 * rows
             attn_f += sel * HQ * 4.0 * D
-        return dict(indexer_flops=flops, topk_bytes=topk_b, attn_bytes=attn_b, attn_flops=attn_f)
+            # tensor-core stage 3: every 128x128 (query, key) tile up to the
+            # diagonal is two MMAs of 2*128*128*D FLOPs per head
+            for qt in range((Tq + 127) // 128):
+                t_end = p["q0"] + min((qt + 1) * 128, Tq)
+                nblk = min((t_end - 1) // 128 + 1, (T + 127) // 128)
+                tile_f += B * HQ * nblk * 4.0 * 128 * 128 * D
+        return dict(indexer_flops=flops, topk_bytes=topk_b, attn_bytes=attn_b, attn_flops=attn_f,
+                    attn_tile_flops=tile_f)
 
 
 # --------------------------------------------------------------------------
@@ -362,7 +381,8 @@ def run_b200(args, cfg, world, rank, local):
     for _ in range(args.warmup):
         pipe.step()
     nb = len(pipe.parts)
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nb)]
+    ns = len(pipe.stage_names)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(ns + 1)] for _ in range(nb)]
            for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
@@ -387,10 +407,10 @@ def run_b200(args, cfg, world, rank, local):
             total_ms += start.elapsed_time(end)
         barrier(world)
     clk = clocks.stop()
-    stage_ms = [0.0, 0.0, 0.0]
+    stage_ms = [0.0] * ns
     for s in range(args.steps):
         for i in range(nb):
-            for j in range(3):
+            for j in range(ns):
                 stage_ms[j] += evs[s][i][j].elapsed_time(evs[s][i][j + 1])
     stage_ms = [x / args.steps for x in stage_ms]
     t_max = max_over_ranks(total_ms, world)
@@ -413,10 +433,16 @@ def run_b200(args, cfg, world, rank, local):
                         traffic=traffic.get("indexer")),
         "topk": dict(bound="hbm", achieved=alg["topk_bytes"] / (stage_ms[1] / 1e3) / 1e9, peak=hbm,
                      unit="GB/s", ms=stage_ms[1], kernel="topk_select_kernel", traffic=traffic.get("topk")),
-        "sparse_attn": dict(bound="hbm", achieved=alg["attn_bytes"] / (stage_ms[2] / 1e3) / 1e9, peak=hbm,
-                            unit="GB/s", ms=stage_ms[2], kernel="sparse_attn_kernel",
+        "sparse_attn": dict(bound="hbm", achieved=alg["attn_bytes"] / (stage_ms[-1] / 1e3) / 1e9, peak=hbm,
+                            unit="GB/s", ms=stage_ms[-1], kernel="sparse_attn_kernel",
                             traffic=traffic.get("sparse_attn")),
     }
+    if pipe.tc:
+        stages["topk"]["kernel"] = "topk_cached_kernel (threshold + kept-set bitmap)"
+        stages["sparse_attn"] = dict(
+            bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_sust,
+            unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc_kernel", traffic=traffic.get("sparse_attn"),
+            note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs")
     for v in stages.values():
         v["frac"] = v["achieved"] / v["peak"]
         v["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"

@@ -42,6 +42,12 @@ def lib() -> ctypes.CDLL:
                                                 f32, i32, p]
         L.dsa_sparse_attn.argtypes = [p, p, i64, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
                                       f32, i32, p]
+        L.dsa_bitmap_words.argtypes = [i64]
+        L.dsa_bitmap_words.restype = i64
+        L.dsa_kept_bitmap.argtypes = [p, p, p, i64, i64, i64, i64, i64, p]
+        L.dsa_topk_select_bitmap.argtypes = [p, i64, i64, i64, i64, i32, i64, p, p, p, i64, p]
+        L.dsa_sparse_attn_bitmap.argtypes = [p, i64, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
+                                             f32, i32, p]
         L.dsa_device_status.argtypes = [p]
         L.dsa_device_status.restype = i32
         L.dsa_forward_workspace_bytes.argtypes = [i64, i64, i64, i64]
@@ -49,7 +55,8 @@ def lib() -> ctypes.CDLL:
         L.dsa_forward.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                   i32, i32, p, sz, p]
         for name in ("dsa_indexer_scores", "dsa_topk_select", "dsa_sparse_attn_threshold",
-                     "dsa_sparse_attn", "dsa_forward"):
+                     "dsa_sparse_attn", "dsa_forward", "dsa_kept_bitmap", "dsa_sparse_attn_bitmap",
+                     "dsa_topk_select_bitmap"):
             getattr(L, name).restype = i32
         _lib = L
     return _lib
@@ -119,6 +126,39 @@ def sparse_attn(idx, cnt, idx_cap, scores, thr, Q, K, V, O, *, q_row0=0, scale=N
     _check(lib().dsa_sparse_attn(_ptr(idx), _ptr(cnt), idx_cap, _ptr(scores), _ptr(thr), _ptr(Q),
                                  _ptr(K), _ptr(V), _ptr(O), B, T_q, T_k, q_row0, HQ, DQ, DV, scale,
                                  dtype_code(Q), _stream()), "dsa_sparse_attn")
+
+
+def bitmap_words(T_k) -> int:
+    return int(lib().dsa_bitmap_words(T_k))
+
+
+def attn_tc_supported(Q, V) -> bool:
+    """Whether dsa_sparse_attn_bitmap runs this dtype / head size (bf16 or fp16, DQ == DV in {64, 128})."""
+    return (Q.dtype in (torch.bfloat16, torch.float16) and Q.shape[-1] == V.shape[-1]
+            and Q.shape[-1] in (64, 128))
+
+
+def kept_bitmap(scores, thr, bits, *, q_row0=0):
+    B, T_q, T_k = scores.shape
+    _check(lib().dsa_kept_bitmap(_ptr(scores), _ptr(thr), _ptr(bits), B, T_q, T_k, q_row0,
+                                 bits.shape[-1], _stream()), "dsa_kept_bitmap")
+
+
+def topk_select_bitmap(scores, k, thr, bits, cnt=None, *, causal=True, q_row0=0):
+    """Threshold (+ count) and kept-set bitmap of every row of scores [B, T_q, T_k]."""
+    B, T_q, T_k = scores.shape
+    _check(lib().dsa_topk_select_bitmap(_ptr(scores), B * T_q, T_k, T_q, q_row0, int(bool(causal)), k,
+                                        _ptr(thr), _ptr(cnt), _ptr(bits), bits.shape[-1], _stream()),
+           "dsa_topk_select_bitmap")
+
+
+def sparse_attn_bitmap(bits, Q, K, V, O, *, q_row0=0, scale=None):
+    B, T_q, HQ, DQ = Q.shape
+    T_k, DV = K.shape[1], V.shape[-1]
+    scale = DQ ** -0.5 if scale is None else scale
+    _check(lib().dsa_sparse_attn_bitmap(_ptr(bits), bits.shape[-1], _ptr(Q), _ptr(K), _ptr(V),
+                                        _ptr(O), B, T_q, T_k, q_row0, HQ, DQ, DV, scale,
+                                        dtype_code(Q), _stream()), "dsa_sparse_attn_bitmap")
 
 
 def device_status() -> int:

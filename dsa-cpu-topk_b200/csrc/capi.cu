@@ -21,11 +21,20 @@ bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype);
 int indexer_tc_take_timeout(cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
                 int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
-                int32_t* idx, int32_t* cnt, int64_t idx_cap, cudaStream_t stream);
+                int32_t* idx, int32_t* cnt, int64_t idx_cap, uint32_t* bits, int64_t words,
+                cudaStream_t stream);
 int fused_small_forward(const void* q_idx, const void* k_idx, const float* w_idx, const void* Q,
                         const void* K, const void* V, float* O, int64_t B, int64_t T_q, int64_t T_k,
                         int64_t q_row0, int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV,
                         int64_t k, int idx_dtype, int qkv_dtype, cudaStream_t stream);
+int64_t bitmap_words(int64_t T_k);
+int kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B, int64_t T_q,
+                int64_t T_k, int64_t q_row0, int64_t words, cudaStream_t stream);
+bool attn_tc_supported(int64_t HQ, int64_t DQ, int64_t DV, int dtype);
+int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, const void* V,
+            float* O, int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t D,
+            float scale, int dtype, cudaStream_t stream);
+int attn_tc_take_timeout(cudaStream_t stream);
 int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const float* scores,
                 const float* thr, const void* Q, const void* K, const void* V, float* O, int64_t B,
                 int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t DQ, int64_t DV,
@@ -71,9 +80,16 @@ static bool force_simt() {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// DSA_ATTN_GATHER=1 keeps bf16/fp16 attention on the gather kernel over the
+// kept lists instead of the tensor-core kernel over the kept-set bitmap.
+static bool force_gather() {
+    const char* e = getenv("DSA_ATTN_GATHER");
+    return e && e[0] == '1';
+}
+
 struct ForwardLayout {
-    size_t scores, thr, cnt, idx, total;
-    int64_t idx_cap;
+    size_t scores, thr, cnt, idx, bits, total;
+    int64_t idx_cap, words;
 };
 
 static ForwardLayout forward_layout(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k) {
@@ -90,6 +106,9 @@ static ForwardLayout forward_layout(int64_t B, int64_t T_q, int64_t T_k, int64_t
     off += align256((size_t)rows * sizeof(int32_t));
     L.idx = off;
     off += align256((size_t)rows * (size_t)L.idx_cap * sizeof(int32_t));
+    L.words = bitmap_words(T_k);
+    L.bits = off;
+    off += align256((size_t)rows * (size_t)L.words * sizeof(uint32_t));
     L.total = off;
     return L;
 }
@@ -143,7 +162,17 @@ int dsa_topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_
                     void* stream) {
     clear_error();
     return topk_select(scores, n_rows, row_len, row_stride, rows_per_batch, q_row0, causal, k,
-                       thr_out, idx_out, cnt_out, idx_cap, (cudaStream_t)stream);
+                       thr_out, idx_out, cnt_out, idx_cap, nullptr, 0, (cudaStream_t)stream);
+}
+
+int dsa_topk_select_bitmap(const float* scores, int64_t n_rows, int64_t row_len,
+                           int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
+                           float* thr_out, int32_t* cnt_out, uint32_t* bits, int64_t words_per_row,
+                           void* stream) {
+    clear_error();
+    if (!bits) return fail(DSA_ERR_INVALID, "topk_select_bitmap: bits is required");
+    return topk_select(scores, n_rows, row_len, row_len, rows_per_batch, q_row0, causal, k, thr_out,
+                       nullptr, cnt_out, 0, bits, words_per_row, (cudaStream_t)stream);
 }
 
 int dsa_sparse_attn_threshold(const float* scores, const float* thr, const void* Q, const void* K,
@@ -168,12 +197,46 @@ int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, con
 int dsa_device_status(void* stream) {
     clear_error();
     const int r = indexer_tc_take_timeout((cudaStream_t)stream);
-    if (r < 0) return fail(DSA_ERR_CUDA, std::string("dsa_device_status: ") +
-                                             cudaGetErrorString(cudaGetLastError()));
+    const int a = attn_tc_take_timeout((cudaStream_t)stream);
+    if (r < 0 || a < 0)
+        return fail(DSA_ERR_CUDA, std::string("dsa_device_status: ") +
+                                      cudaGetErrorString(cudaGetLastError()));
     if (r > 0)
         return fail(DSA_ERR_TIMEOUT, "a tensor-core indexer launch timed out waiting on its pipeline "
                                      "(its scores are incomplete)");
+    if (a > 0)
+        return fail(DSA_ERR_TIMEOUT, "a tensor-core attention launch timed out waiting on its "
+                                     "pipeline (its output is incomplete)");
     return DSA_OK;
+}
+
+int64_t dsa_bitmap_words(int64_t T_k) { return T_k < 1 ? 0 : bitmap_words(T_k); }
+
+int dsa_kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B, int64_t T_q,
+                    int64_t T_k, int64_t q_row0, int64_t words_per_row, void* stream) {
+    clear_error();
+    return kept_bitmap(scores, thr, bits, B, T_q, T_k, q_row0, words_per_row, (cudaStream_t)stream);
+}
+
+int dsa_sparse_attn_bitmap(const uint32_t* bits, int64_t words_per_row, const void* Q, const void* K,
+                           const void* V, float* O, int64_t B, int64_t T_q, int64_t T_k,
+                           int64_t q_row0, int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                           int dtype, void* stream) {
+    clear_error();
+    if (!bits || !Q || !K || !V || !O) return fail(DSA_ERR_INVALID, "sparse_attn_bitmap: null pointer");
+    if (B < 0 || T_q < 0 || T_k < 1 || q_row0 < 0 || HQ < 1 || DQ < 1 || DV < 1)
+        return fail(DSA_ERR_INVALID, "sparse_attn_bitmap: bad sizes");
+    if (words_per_row < bitmap_words(T_k) || (words_per_row & 3))
+        return fail(DSA_ERR_INVALID, "sparse_attn_bitmap: words_per_row must be a multiple of 4 and "
+                                     ">= dsa_bitmap_words(T_k)");
+    if (!attn_tc_supported(HQ, DQ, DV, dtype))
+        return fail(DSA_ERR_UNSUPPORTED, "sparse_attn_bitmap: needs bf16/fp16 with DQ == DV in {64, 128}");
+    const int rc = attn_tc(bits, words_per_row, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ, scale, dtype,
+                           (cudaStream_t)stream);
+    if (rc == -100)
+        return fail(DSA_ERR_UNSUPPORTED, "sparse_attn_bitmap: shape or alignment outside the "
+                                         "tensor-core kernel's limits");
+    return rc;
 }
 
 size_t dsa_forward_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k) {
@@ -217,11 +280,21 @@ int dsa_forward(const void* q_idx, const void* k_idx, const float* w_idx, const 
     rc = run_indexer(q_idx, k_idx, w_idx, scores, B, T_q, T_k, q_row0, HI, DI, idx_dtype,
                      /*fill_upper=*/0, st);
     if (rc) return rc;
+    const float scale = 1.0f / sqrtf((float)DQ);
+    if (attn_tc_supported(HQ, DQ, DV, qkv_dtype) && !force_gather()) {
+        // threshold and kept-set bitmap, then tensor-core attention
+        uint32_t* bits = reinterpret_cast<uint32_t*>(ws + L.bits);
+        rc = topk_select(scores, B * T_q, T_k, T_k, T_q, q_row0, /*causal=*/1, k, thr, nullptr,
+                         nullptr, 0, bits, L.words, st);
+        if (rc) return rc;
+        rc = attn_tc(bits, L.words, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ, scale, qkv_dtype, st);
+        if (rc != -100) return rc;
+    }
     rc = topk_select(scores, B * T_q, T_k, T_k, T_q, q_row0, /*causal=*/1, k, thr, idx, cnt,
-                     L.idx_cap, st);
+                     L.idx_cap, nullptr, 0, st);
     if (rc) return rc;
     return sparse_attn(idx, cnt, L.idx_cap, scores, thr, Q, K, V, O, B, T_q, T_k, q_row0, HQ, DQ,
-                       DV, 1.0f / sqrtf((float)DQ), qkv_dtype, st);
+                       DV, scale, qkv_dtype, st);
 }
 
 }  // extern "C"

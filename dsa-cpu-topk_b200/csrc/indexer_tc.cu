@@ -31,12 +31,15 @@
 #include <stdlib.h>
 
 #include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace dsa {
 
 __device__ int g_indexer_tc_timeout = 0;
 
 namespace {
+
+using namespace tc;
 
 constexpr int BM = 128;            // query rows per tile (TMEM lanes)
 constexpr int BN = 256;            // keys per tile (MMA N, TMEM columns per accumulator)
@@ -59,136 +62,6 @@ struct TcParams {
     int stall;                  // test hook: the producer issues no loads, so every wait times out
     unsigned long long timeout_ns;
 };
-
-// ---- PTX wrappers ----------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait for the phase of parity `parity` to complete.  Gives up when
-// another warp of the CTA has given up (*abort), or after timeout_ns of
-// device time; then it sets *abort and the sticky device flag that
-// dsa_device_status() reports, and the caller leaves its loop.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
-                                          uint64_t timeout_ns) {
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; ++i) {
-        if (mbar_try_wait(b, parity)) return true;
-        if ((i & 255u) == 255u) {
-            if (*abort) return false;
-            const uint64_t now = global_ns();
-            if (t0 == 0) t0 = now;
-            else if (now - t0 > timeout_ns) {
-                *abort = 1;
-                atomicExch(&g_indexer_tc_timeout, 1);
-                return false;
-            }
-        }
-    }
-}
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
-                                            int c1, int c2) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3, %4}], [%5];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
-                                            int c1, int c2, int c3) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
-        : "memory");
-}
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,
-// 8-row core groups 1024 bytes apart (SBO), sm_100 descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;             // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;   // SBO
-    d |= (uint64_t)1 << 46;             // version
-    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
-    return d;
-}
-// D (TMEM, fp32) (+)= A * B^T for one 32-byte K slice: bf16 (kind::f16,
-// K=16) or e4m3 (kind::f8f6f4, K=32)
-template <bool FP8>
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                     uint32_t accumulate) {
-    if constexpr (FP8) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-    } else {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-    }
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// 16 columns of this warp's TMEM lane quarter, one 32-bit value per column.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-        "%12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-// Wait for this thread's outstanding tcgen05.ld.  The registers of the load
-// whose values are used next are passed through, so no use of them can be
-// scheduled before the wait.
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
-                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
-                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-                 :
-                 : "memory");
-}
 
 // tile index -> (batch, query block, key block) through the per-batch prefix
 // of key blocks per query block
@@ -279,14 +152,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
                 int b, i, j;
                 decode_tile(lin, pref, p, b, i, j);
-                if (!(ok = mbar_wait(&emptyB[bs], bph ^ 1, &s_abort, p.timeout_ns))) break;
+                if (!(ok = mbar_wait(&emptyB[bs], bph ^ 1, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
                 if (!p.stall) mbar_expect_tx(&fullB[bs], p.b_bytes);
                 for (int c = 0; c < nch && !p.stall; ++c)
                     tma_load_3d(sB + (size_t)bs * p.b_bytes + (size_t)c * BN * 128, &tmk, &fullB[bs],
                                 c * kch, j * BN, b);
                 if (++bs == p.nB) { bs = 0; bph ^= 1; }
                 for (int h = 0; h < p.HI; ++h) {
-                    if (!(ok = mbar_wait(&emptyA[as], aph ^ 1, &s_abort, p.timeout_ns))) break;
+                    if (!(ok = mbar_wait(&emptyA[as], aph ^ 1, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
                     if (!p.stall) mbar_expect_tx(&fullA[as], p.a_bytes);
                     for (int c = 0; c < nch && !p.stall; ++c)
                         tma_load_4d(sA + (size_t)as * p.a_bytes + (size_t)c * BM * 128, &tmq,
@@ -307,11 +180,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t aph = 0, bph = 0, tph = 0;
             bool ok = true;
             for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
-                if (!(ok = mbar_wait(&fullB[bs], bph, &s_abort, p.timeout_ns))) break;
+                if (!(ok = mbar_wait(&fullB[bs], bph, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
                 const uint32_t bbase = smem_u32(sB + (size_t)bs * p.b_bytes);
                 for (int h = 0; h < p.HI; ++h) {
-                    if (!(ok = mbar_wait(&fullA[as], aph, &s_abort, p.timeout_ns))) break;
-                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, &s_abort, p.timeout_ns))) break;
+                    if (!(ok = mbar_wait(&fullA[as], aph, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
+                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
                     tc_fence_after();
                     const uint32_t abase = smem_u32(sA + (size_t)as * p.a_bytes);
                     const uint32_t d = tmem_base + (uint32_t)(tb * BN);
@@ -363,7 +236,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (h >= p.HI) break;
                     const float wj = wpre[u];
                     wpre[u] = (row_ok && h + 2 < p.HI) ? __ldg(wrow + h + 2) : 0.f;
-                    if (!(ok = mbar_wait(&tfull[tb], tph, &s_abort, p.timeout_ns))) break;
+                    if (!(ok = mbar_wait(&tfull[tb], tph, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
                     tc_fence_after();
                     const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + half * 128);
                     // 16-column chunks, the next chunk's load in flight while the
@@ -450,39 +323,10 @@ bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype) {
     return false;
 }
 
-// cuTensorMapEncodeTiled is looked up through the runtime, so the library
-// does not link libcuda (it loads on hosts without a driver).
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(f);
-    }
-    return fn;
-}
-
 static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
                       const cuuint64_t* strides, const cuuint32_t* box, const char* what, int elt) {
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return fail(DSA_ERR_CUDA, "indexer_tc: cuTensorMapEncodeTiled not available");
-    const CUresult r = enc(
-        m, elt == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
-        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return fail(DSA_ERR_CUDA, std::string("indexer_tc: cuTensorMapEncodeTiled failed for ") + what +
-                                      " (" + std::to_string((int)r) + ")");
-    return DSA_OK;
+    return tc::encode_map(m, base, rank, dims, strides, box, std::string("indexer_tc: ") + what,
+                          elt == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
 }
 
 int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,

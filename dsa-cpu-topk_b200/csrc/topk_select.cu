@@ -35,6 +35,8 @@ struct TopkArgs {
     int32_t* idx;
     int32_t* cnt;
     int64_t idx_cap;
+    uint32_t* bits;     // kept-set bitmap [n_rows, words] (CTA-per-row kernel only), or null
+    int64_t words;
     int cache_elems;
     int cand_max;
     int vec_ok;
@@ -309,6 +311,38 @@ __device__ __forceinline__ uint4 group_keys(const uint4* cache4, const float* sr
     }
 }
 
+// Kept-set bitmap of one row: bit s % 32 of word s / 32 is set iff s < valid
+// and key(s) >= thr_key (every s < valid when `all`).  Each thread turns one
+// float4 group into a nibble and eight lanes OR theirs into a word; words is
+// a multiple of 4, so every warp runs the same number of iterations.
+template <int BLOCK, bool CACHED>
+__device__ __forceinline__ void emit_bits(const TopkArgs& a, int64_t row, const float* src,
+                                          const uint4* cache4, int valid, uint32_t thr_key, bool all) {
+    uint32_t* out = a.bits + row * a.words;
+    const int ng = (int)a.words * 8;
+    const int g4 = (valid + 3) >> 2;
+    const int lane = threadIdx.x & 31;
+    for (int g = threadIdx.x; g < ng; g += BLOCK) {
+        uint32_t nib = 0;
+        if (g < g4) {
+            if (all) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) nib |= (uint32_t)(4 * g + j < valid) << j;
+            } else {
+                // keys past `valid` are 0, below every real key
+                const uint4 kk = group_keys<CACHED>(cache4, src, g, valid, a.vec_ok);
+                nib = (uint32_t)(kk.x >= thr_key) | (uint32_t)(kk.y >= thr_key) << 1 |
+                      (uint32_t)(kk.z >= thr_key) << 2 | (uint32_t)(kk.w >= thr_key) << 3;
+            }
+        }
+        uint32_t w = nib << (4 * (lane & 7));
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        w |= __shfl_xor_sync(0xffffffffu, w, 2);
+        w |= __shfl_xor_sync(0xffffffffu, w, 4);
+        if ((lane & 7) == 0) out[g >> 3] = w;
+    }
+}
+
 template <int BLOCK, bool CACHED>
 __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
     constexpr int NW = BLOCK / 32;
@@ -341,6 +375,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
                 const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
                 for (int i = tid; i < n; i += BLOCK) a.idx[row * a.idx_cap + i] = i;
             }
+            if (a.bits) emit_bits<BLOCK, CACHED>(a, row, src, dyn4, valid, 0u, true);
             continue;
         }
         const int g4 = (valid + 3) >> 2;  // uint4 groups; padding keys are 0
@@ -543,6 +578,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
                 base += __shfl_sync(0xffffffffu, pre, 31);
             }
         }
+        if (a.bits) emit_bits<BLOCK, CACHED>(a, row, src, dyn4, valid, thr_key, false);
         __syncthreads();
     }
 }
@@ -883,9 +919,16 @@ int launch_warp_l2(const TopkArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
+int kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B, int64_t T_q,
+                int64_t T_k, int64_t q_row0, int64_t words, cudaStream_t stream);
+int64_t bitmap_words(int64_t T_k);
+
+static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream);
+
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
                 int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
-                int32_t* idx, int32_t* cnt, int64_t idx_cap, cudaStream_t stream) {
+                int32_t* idx, int32_t* cnt, int64_t idx_cap, uint32_t* bits, int64_t words,
+                cudaStream_t stream) {
     if (n_rows < 0 || row_len < 1 || row_stride < row_len)
         return fail(DSA_ERR_INVALID, "topk_select: need n_rows >= 0, row_len >= 1, row_stride >= row_len");
     if (k < 1 || k > row_len)
@@ -896,6 +939,9 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     if (q_row0 < 0) return fail(DSA_ERR_INVALID, "topk_select: q_row0 < 0");
     if (!scores || !thr) return fail(DSA_ERR_INVALID, "topk_select: scores and thr_out are required");
     if (idx && idx_cap < 1) return fail(DSA_ERR_INVALID, "topk_select: idx_cap < 1 with idx_out");
+    if (bits && (words < bitmap_words(row_len) || (words & 3) || row_stride != row_len))
+        return fail(DSA_ERR_INVALID, "topk_select: the bitmap needs words_per_row a multiple of 4, >= "
+                                     "dsa_bitmap_words(row_len), and row_stride == row_len");
     if (n_rows == 0) return DSA_OK;
 
     TopkArgs a;
@@ -911,6 +957,8 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     a.idx = idx;
     a.cnt = cnt;
     a.idx_cap = idx ? idx_cap : 0;
+    a.bits = nullptr;
+    a.words = words;
     a.vec_ok = (aligned16(scores) && row_stride % 4 == 0) ? 1 : 0;
     // longest row any CTA will see
     int64_t longest = row_len;
@@ -920,6 +968,19 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     }
     constexpr int64_t kCacheMax = 12288;  // 48 KB of keys per CTA
     a.cache_elems = (int)(longest < kCacheMax ? longest : kCacheMax);
+    // the CTA-per-row kernel writes the bitmap in its last sweep; rows the
+    // other kernels take get it from kept_bitmap_kernel afterwards
+    const bool cta_kernel = longest > 4096 && longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH");
+    if (bits && cta_kernel) a.bits = bits;
+    int rc = topk_launch(a, longest, stream);
+    if (rc || !bits || cta_kernel) return rc;
+    // causal rows: key s kept only if s <= q_row0 + r % rows_per_batch;
+    // otherwise a q_row0 past the row end makes every position causal
+    return kept_bitmap(scores, thr, bits, n_rows / a.rows_per_batch, a.rows_per_batch, row_len,
+                       causal ? q_row0 : row_len, words, stream);
+}
+
+static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream) {
     // rows <= 512: one warp per row (measured 2.6-2.9x faster than a CTA per
     // row there; slower than it on 1K-2K rows, where the CTA kernel is kept)
     if (longest <= 512 && !getenv("DSA_TOPK_LONG_PATH") && !getenv("DSA_TOPK_NO_WARP")) {

@@ -25,6 +25,7 @@ power-of-two and T <= ~512 limits are lifted; its other assertions
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -94,8 +95,36 @@ def sparse_attention_with_threshold_triton(scores, threshold, Q, K, V) -> torch.
     scores = _native.prep(scores.float())
     threshold = _native.prep(threshold.float())
     Q, K, V = _native.prep(Q), _native.prep(K), _native.prep(V)
+    if _native.attn_tc_supported(Q, V) and os.environ.get("DSA_ATTN_GATHER") != "1":
+        # tensor cores: the kept set as a bitmap, then the masked flash attention
+        return sparse_attention_with_bitmap(kept_bitmap(scores, threshold), Q, K, V)
     out = torch.empty(B, T, HQ, DV, device=Q.device, dtype=torch.float32)
     _native.sparse_attn_threshold(scores, threshold, Q, K, V, out, scale=1.0 / math.sqrt(DQ))
+    return out
+
+
+def kept_bitmap(scores, threshold, *, q_row0: int = 0) -> torch.Tensor:
+    """Kept set of each query row as bits: [B*T_q, dsa_bitmap_words(T_k)] int32.
+
+    Bit s % 32 of word s // 32 of row b*T_q + i is set iff s <= q_row0 + i and
+    scores[b, i, s] >= threshold[b, i] (the mask of dsa_attention.py:262-266).
+    """
+    B, T_q, T_k = scores.shape
+    scores = _native.prep(scores.float())
+    threshold = _native.prep(threshold.float())
+    bits = torch.empty(B * T_q, _native.bitmap_words(T_k), device=scores.device, dtype=torch.int32)
+    _native.kept_bitmap(scores, threshold, bits, q_row0=q_row0)
+    return bits
+
+
+def sparse_attention_with_bitmap(bits, Q, K, V, *, q_row0: int = 0) -> torch.Tensor:
+    """Attention over the set bits of kept_bitmap, on the tensor cores (bf16/fp16, D in {64, 128})."""
+    B, T_q, HQ, DQ = Q.shape
+    DV = V.shape[-1]
+    Q, K, V = _native.prep(Q), _native.prep(K), _native.prep(V)
+    out = torch.empty(B, T_q, HQ, DV, device=Q.device, dtype=torch.float32)
+    _native.sparse_attn_bitmap(_native.prep(bits), Q, K, V, out, q_row0=q_row0,
+                               scale=1.0 / math.sqrt(DQ))
     return out
 
 

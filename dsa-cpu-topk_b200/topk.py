@@ -53,6 +53,24 @@ def topk_select(scores: torch.Tensor, k: int, *, causal: bool = False, q_row0: i
     return thr, idx, cnt
 
 
+def topk_select_bitmap(scores: torch.Tensor, k: int, *, causal: bool = True, q_row0: int = 0):
+    """scores [B, T_q, N] fp32 CUDA -> (thr [rows], cnt [rows] int32, bits [rows, words] int32).
+
+    The kept set of each row (score >= thr, and s <= q_row0 + t when causal)
+    as the bitmap of dsa_attention.kept_bitmap, written by the top-K kernel
+    itself where the row length allows (4K-32K entries)."""
+    assert scores.is_cuda and scores.dtype == torch.float32 and scores.dim() == 3, \
+        "scores must be fp32 CUDA [B, T_q, N]"
+    B, T_q, N = scores.shape
+    assert 1 <= k <= N, f"need 1 <= k <= N (k={k}, N={N})"
+    s = _native.prep(scores)
+    thr = torch.empty(B * T_q, device=s.device, dtype=torch.float32)
+    cnt = torch.empty(B * T_q, device=s.device, dtype=torch.int32)
+    bits = torch.empty((B * T_q, _native.bitmap_words(N)), device=s.device, dtype=torch.int32)
+    _native.topk_select_bitmap(s, k, thr, bits, cnt, causal=causal, q_row0=q_row0)
+    return thr, cnt, bits
+
+
 def topk_threshold(scores: torch.Tensor, k: int) -> torch.Tensor:
     """[..., N] fp32 -> [..., 1] k-th largest per row (topk_avx512.cpp:226-253 contract)."""
     assert k > 0, "k must be > 0"

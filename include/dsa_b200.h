@@ -27,6 +27,10 @@
  *                              topk_avx512.cpp:226-257       topk_threshold / topk_threshold_batch_merge
  *   dsa_sparse_attn_threshold  dsa_attention.py:298-324      sparse_attention_with_threshold_triton
  *   dsa_sparse_attn            dsa_attention.py:72-87        (gather form of the selection, naive variant)
+ *   dsa_kept_bitmap,           dsa_attention.py:230-324      _sparse_attn_threshold_kernel: its per-tile
+ *   dsa_topk_select_bitmap,                                  mask (scores >= thr, s <= t) as a bitmap, and
+ *   dsa_sparse_attn_bitmap
+ *                                                            the masked flash attention on the tensor cores
  *   dsa_forward                dsa_attention.py:327-344      dsa_attention_split_triton (and the fused
  *                              dsa_attention.py:196-227      dsa_attention_triton, same result)
  */
@@ -138,12 +142,50 @@ DSA_API int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_
                     int dtype, void* stream);
 
 /*
+ * Stage 3 (bitmap form, tensor cores) — the kept set as one bit per
+ * (query row, key), then a masked flash attention over it.
+ *   dsa_bitmap_words(T_k): words per bitmap row, ceil(T_k/128)*4.
+ *   dsa_kept_bitmap: bits [B*T_q, words_per_row] uint32 out; bit (s & 31) of
+ *     word s/32 of row r is 1 iff s <= q_row0 + r % T_q and scores[r,s] >= thr[r]
+ *     (scores, thr as in dsa_sparse_attn_threshold).  words_per_row must be a
+ *     multiple of 4 and >= dsa_bitmap_words(T_k); words past T_k are zero.
+ *   dsa_sparse_attn_bitmap: attention of each query over its set bits,
+ *     O [B, T_q, HQ, DV] fp32 out; Q/K/V as in dsa_sparse_attn_threshold.
+ *     bf16 or fp16 with DQ == DV in {64, 128}, else DSA_ERR_UNSUPPORTED.
+ *     The softmax weights enter the P.V product rounded to the input dtype;
+ *     results agree with the fp32 threshold form to the dtype's tolerance.
+ */
+DSA_API int64_t dsa_bitmap_words(int64_t T_k);
+
+DSA_API int dsa_kept_bitmap(const float* scores, const float* thr, uint32_t* bits,
+                            int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                            int64_t words_per_row, void* stream);
+
+/* Stage 2 writing the kept set as the bitmap of dsa_kept_bitmap instead of
+ * index lists (rows with row_stride == row_len).  Same selection as
+ * dsa_topk_select; cnt_out may be NULL.  Rows of 4K-32K entries get the bitmap
+ * from the top-K kernel's last sweep, others from a dsa_kept_bitmap pass. */
+DSA_API int dsa_topk_select_bitmap(const float* scores, int64_t n_rows, int64_t row_len,
+                                   int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
+                                   float* thr_out, int32_t* cnt_out, uint32_t* bits,
+                                   int64_t words_per_row, void* stream);
+
+DSA_API int dsa_sparse_attn_bitmap(const uint32_t* bits, int64_t words_per_row,
+                                   const void* Q, const void* K, const void* V, float* O,
+                                   int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                                   int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                                   int dtype, void* stream);
+
+/*
  * Whole forward (stage 1 -> 2 -> 3) in caller-provided workspace.
  * idx_dtype is the dtype of q_idx/k_idx, qkv_dtype that of Q/K/V; w_idx is fp32.
  * Layouts as above: q_idx [B,T_q,HI,DI], k_idx [B,T_k,DI], w_idx [B,T_q,HI],
  * Q [B,T_q,HQ,DQ], K [B,T_k,HQ,DQ], V [B,T_k,HQ,DV], O [B,T_q,HQ,DV] fp32.
  * top_k is clamped to T_k (k_eff = min(k, T), dsa_attention.py:41).
  * workspace must hold dsa_forward_workspace_bytes(...) bytes, 256-byte aligned.
+ * Stage 3 runs on the tensor cores (threshold -> bitmap -> dsa_sparse_attn_bitmap)
+ * when qkv_dtype is bf16/fp16 with DQ == DV in {64, 128}, else as the gather
+ * over the kept lists (dsa_sparse_attn).
  */
 DSA_API size_t dsa_forward_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k);
 

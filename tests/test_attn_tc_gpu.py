@@ -1,0 +1,167 @@
+"""GPU: the tensor-core attention stage (kept-set bitmap + tcgen05 masked
+flash attention) against the oracle.
+
+The bitmap is integer work and must match bit for bit.  The attention rounds
+its softmax weights to the input dtype before the P.V product, so it is held
+to the north-star bf16/fp16 tolerance (2e-2 relative to max(1, |O|max)), and
+it is also compared with the fp32 gather kernel on identical kept sets."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import dsa_oracle as o
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits_ref(sc: torch.Tensor, thr: torch.Tensor, q_row0: int, words: int) -> np.ndarray:
+    """Bitmap of (s <= q_row0 + i) & (scores >= thr), built with numpy."""
+    B, T_q, T_k = sc.shape
+    t = q_row0 + torch.arange(T_q).view(1, T_q, 1)
+    s = torch.arange(T_k).view(1, 1, T_k)
+    keep = ((s <= t) & (sc >= thr.view(B, T_q, 1))).reshape(B * T_q, T_k).numpy()
+    pad = np.zeros((B * T_q, words * 32), dtype=np.uint64)
+    pad[:, :T_k] = keep
+    w = (pad.reshape(B * T_q, words, 32) << np.arange(32, dtype=np.uint64)).sum(-1)
+    return w.astype(np.uint32).view(np.int32)
+
+
+def _case(B, T_q, T_k, HQ, D, k, dtype, q_row0, seed):
+    g = torch.Generator().manual_seed(seed)
+    sc = torch.randn(B, T_q, T_k, generator=g)
+    # ties: quantise a third of the rows so equal scores straddle the threshold
+    sc[:, ::3] = (sc[:, ::3] * 4).round() / 4
+    t = q_row0 + torch.arange(T_q).view(1, T_q, 1)
+    causal = torch.arange(T_k).view(1, 1, T_k) <= t
+    masked = torch.where(causal, sc, torch.full_like(sc, -math.inf))
+    kk = min(k, T_k)
+    thr = masked.topk(kk, dim=-1).values[..., -1]
+    # rows with fewer than k causal keys keep all of them
+    thr = torch.where(torch.isfinite(thr), thr, torch.full_like(thr, -math.inf))
+    Q = torch.randn(B, T_q, HQ, D, generator=g).to(dtype)
+    K = torch.randn(B, T_k, HQ, D, generator=g).to(dtype)
+    V = torch.randn(B, T_k, HQ, D, generator=g).to(dtype)
+    return sc, thr, Q, K, V
+
+
+def _oracle(sc, thr, Q, K, V, q_row0):
+    """fp32 attention over the kept set of each row (the oracle's _attend rule)."""
+    B, T_q, T_k = sc.shape
+    D = Q.shape[-1]
+    t = q_row0 + torch.arange(T_q).view(1, T_q, 1)
+    keep = (torch.arange(T_k).view(1, 1, T_k) <= t) & (sc >= thr.view(B, T_q, 1))
+    logits = torch.einsum("bthd,bshd->bhts", Q.float(), K.float()) / math.sqrt(D)
+    logits = logits.masked_fill(~keep.unsqueeze(1), -math.inf)
+    p = torch.softmax(logits, dim=-1)
+    return torch.einsum("bhts,bshd->bthd", p, V.float())
+
+
+CASES = [
+    # B, T_q, T_k, HQ, D, k, dtype, q_row0
+    (1, 256, 256, 2, 128, 32, torch.bfloat16, 0),
+    (2, 300, 300, 3, 64, 40, torch.bfloat16, 0),      # ragged tiles, D=64
+    (1, 200, 777, 2, 128, 64, torch.float16, 577),    # a row block at an offset, T_k ragged
+    (1, 1024, 1024, 4, 128, 96, torch.bfloat16, 0),
+    (2, 513, 513, 2, 64, 513, torch.float16, 0),      # k >= T: dense causal attention
+    (1, 64, 4000, 1, 128, 300, torch.bfloat16, 3936), # one short query tile, many key blocks
+]
+
+
+@pytest.mark.parametrize("B,T_q,T_k,HQ,D,k,dtype,q_row0", CASES)
+def test_bitmap_and_tc_attention_match_oracle(cuda, B, T_q, T_k, HQ, D, k, dtype, q_row0):
+    import _native
+    from dsa_attention import kept_bitmap, sparse_attention_with_bitmap
+    sc, thr, Q, K, V = _case(B, T_q, T_k, HQ, D, k, dtype, q_row0, seed=T_q + T_k + D)
+    bits = kept_bitmap(sc.to(cuda), thr.to(cuda), q_row0=q_row0)
+    words = _native.bitmap_words(T_k)
+    assert bits.shape == (B * T_q, words) and words % 4 == 0
+    assert np.array_equal(bits.cpu().numpy(), _bits_ref(sc, thr, q_row0, words))
+    out = sparse_attention_with_bitmap(bits, Q.to(cuda), K.to(cuda), V.to(cuda), q_row0=q_row0).cpu()
+    ref = _oracle(sc, thr, Q, K, V, q_row0)
+    assert torch.isfinite(out).all()
+    err = (out - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), err
+
+
+def test_tc_attention_agrees_with_gather_kernel(cuda, monkeypatch):
+    """Same kept sets through both stage-3 kernels (bitmap/tensor cores vs threshold/gather)."""
+    from dsa_attention import sparse_attention_with_threshold_triton
+    sc, thr, Q, K, V = _case(2, 640, 640, 4, 128, 64, torch.bfloat16, 0, seed=11)
+    args = (sc.to(cuda), thr.to(cuda), Q.to(cuda), K.to(cuda), V.to(cuda))
+    tc = sparse_attention_with_threshold_triton(*args)
+    monkeypatch.setenv("DSA_ATTN_GATHER", "1")
+    ga = sparse_attention_with_threshold_triton(*args)
+    assert (tc - ga).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("B,T,HI,DI,HQ,D,k,dtype", [
+    (1, 1024, 8, 128, 4, 128, 64, torch.bfloat16),
+    (2, 700, 4, 64, 2, 64, 50, torch.float16),
+])
+def test_forward_tc_path_matches_oracle_and_gather(cuda, B, T, HI, DI, HQ, D, k, dtype, monkeypatch):
+    from dsa_attention import dsa_forward
+    args = [x.to(cuda) for x in o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype, seed0=5)]
+    out = dsa_forward(*args, k)
+    monkeypatch.setenv("DSA_ATTN_GATHER", "1")
+    ga = dsa_forward(*args, k)
+    assert (out - ga).abs().max().item() <= 2e-2
+    ref = o.dsa_attention(*(a.cpu() for a in args), k)
+    assert (out.cpu() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+def test_bitmap_entry_points_reject_bad_arguments(cuda):
+    import _native
+    from dsa_attention import sparse_attention_with_bitmap
+    Q = torch.zeros(1, 128, 1, 32, device=cuda, dtype=torch.bfloat16)   # D=32: not on the tensor cores
+    bits = torch.zeros(128, _native.bitmap_words(128), device=cuda, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="bf16/fp16"):
+        sparse_attention_with_bitmap(bits, Q, Q, Q)
+    sc = torch.zeros(1, 128, 128, device=cuda)
+    thr = torch.zeros(128, device=cuda)
+    short = torch.zeros(128, 2, device=cuda, dtype=torch.int32)          # fewer words than needed
+    with pytest.raises(AssertionError, match="words_per_row"):
+        _native.kept_bitmap(sc, thr, short)
+
+
+def test_attention_wait_timeout_is_reported_and_recoverable(cuda, monkeypatch):
+    """Test hook DSA_TEST_ATTN_STALL: the producer issues no loads, every wait
+    runs out after 20 ms, the kernel returns and the status reports it."""
+    import _native
+    from dsa_attention import kept_bitmap, sparse_attention_with_bitmap
+    sc, thr, Q, K, V = _case(1, 256, 256, 2, 64, 32, torch.bfloat16, 0, seed=3)
+    bits = kept_bitmap(sc.to(cuda), thr.to(cuda))
+    Q, K, V = Q.to(cuda), K.to(cuda), V.to(cuda)
+    assert _native.device_status() == _native.DSA_OK
+    monkeypatch.setenv("DSA_TEST_ATTN_STALL", "1")
+    sparse_attention_with_bitmap(bits, Q, K, V)
+    assert _native.device_status() == _native.DSA_ERR_TIMEOUT
+    assert _native.device_status() == _native.DSA_OK
+    monkeypatch.delenv("DSA_TEST_ATTN_STALL")
+    out = sparse_attention_with_bitmap(bits, Q, K, V).cpu()
+    assert _native.device_status() == _native.DSA_OK
+    ref = _oracle(sc, thr, Q.cpu(), K.cpu(), V.cpu(), 0)
+    assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("B,T_q,T_k,k,q_row0,causal", [
+    (1, 64, 6000, 700, 5936, True),     # 4K-32K rows: the bitmap comes from the top-K kernel
+    (2, 40, 9000, 64, 8960, True),
+    (1, 300, 300, 20, 0, True),         # short rows: top-K kernel, then the bitmap kernel
+    (3, 5, 5000, 100, 0, False),        # full rows, no causal limit
+])
+def test_topk_bitmap_equals_threshold_then_bitmap(cuda, B, T_q, T_k, k, q_row0, causal):
+    from dsa_attention import kept_bitmap
+    from topk import topk_select, topk_select_bitmap
+    g = torch.Generator(device=cuda).manual_seed(T_k)
+    sc = torch.randn(B, T_q, T_k, generator=g, device=cuda)
+    sc[:, ::2] = (sc[:, ::2] * 8).round() / 8            # ties at the threshold
+    thr, cnt, bits = topk_select_bitmap(sc, k, causal=causal, q_row0=q_row0)
+    thr2, _, cnt2 = topk_select(sc, k, causal=causal, q_row0=q_row0, idx_cap=32)
+    assert torch.equal(thr, thr2) and torch.equal(cnt, cnt2)
+    if causal:
+        ref = kept_bitmap(sc, thr, q_row0=q_row0)
+    else:
+        ref = torch.from_numpy(_bits_ref(sc.cpu(), thr.cpu(), T_k, bits.shape[1])).to(cuda)
+    assert torch.equal(bits, ref)

@@ -43,15 +43,26 @@ def test_forward_matches_reference_golden(cuda, name):
 
 
 @pytest.mark.parametrize("name", NAMES)
-def test_threshold_form_matches_oracle(cuda, name):
-    """Stage 3 alone on the reference's own scores and thresholds."""
+def test_threshold_form_matches_oracle(cuda, name, monkeypatch):
+    """Stage 3 alone on the reference's own scores and thresholds.
+
+    The gather kernel computes in fp32 on the upcast inputs like the
+    reference (1e-4 fp32, 1e-3 bf16).  For bf16 heads of 64/128 the default
+    path is the tensor-core kernel, which rounds the softmax weights to bf16
+    before P.V: it is held to the bf16 bar, 2e-2 of max(1, |O|)."""
+    import _native
     from dsa_attention import sparse_attention_with_threshold_triton
     d = golden(name)
     args, dt = inputs(d, cuda)
     sc = o.indexer_scores(*(a.cpu() for a in args[:3]))
     thr = t(d["thr"])
-    out = sparse_attention_with_threshold_triton(sc.to(cuda), thr.to(cuda), *args[3:]).cpu()
     ref = o.sparse_attention_with_threshold(sc, thr, *(a.cpu() for a in args[3:]))
+    out = sparse_attention_with_threshold_triton(sc.to(cuda), thr.to(cuda), *args[3:]).cpu()
+    tc = _native.attn_tc_supported(args[3], args[5])
+    tol = 2e-2 * max(1.0, ref.abs().max().item()) if tc else (1e-4 if dt == torch.float32 else 1e-3)
+    assert (out - ref).abs().max() < tol
+    monkeypatch.setenv("DSA_ATTN_GATHER", "1")
+    out = sparse_attention_with_threshold_triton(sc.to(cuda), thr.to(cuda), *args[3:]).cpu()
     assert (out - ref).abs().max() < (1e-4 if dt == torch.float32 else 1e-3)
 
 
@@ -81,13 +92,20 @@ def test_list_form_overflow_rows_fall_back(cuda):
     (1, 300, 4, 32, 2, 128, 16, torch.float32),    # D = 128 fp32
     (1, 300, 4, 32, 8, 256, 16, torch.bfloat16),   # D = 256 bf16 (1024-thread rows)
 ])
-def test_forward_random(cuda, B, T, HI, DI, HQ, D, k, dtype):
-    """End to end against the oracle, with the selection checked on the GPU's own scores."""
+def test_forward_random(cuda, B, T, HI, DI, HQ, D, k, dtype, monkeypatch):
+    """End to end against the oracle, with the selection checked on the GPU's own scores.
+
+    The elementwise bounds hold for the fp32-arithmetic gather kernel.  bf16/fp16
+    heads of 64/128 also run the default tensor-core stage 3, whose bf16 softmax
+    weights are held to 2e-2 of max(1, |O|)."""
+    import _native
     from dsa_attention import dsa_forward
     from lightning_indexer import indexer_scores
     from topk import topk_select
     qi, ki, wi, Q, K, V = o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype)
     dev = [x.to(cuda) for x in (qi, ki, wi, Q, K, V)]
+    tc_out = dsa_forward(*dev, min(k, T)).cpu() if _native.attn_tc_supported(Q, V) else None
+    monkeypatch.setenv("DSA_ATTN_GATHER", "1")
     out = dsa_forward(*dev, min(k, T)).cpu()
     # the GPU's own scores -> oracle selection -> oracle attention
     sc = indexer_scores(*dev[:3]).cpu()
@@ -103,6 +121,8 @@ def test_forward_random(cuda, B, T, HI, DI, HQ, D, k, dtype):
     ref2 = o.dsa_attention(qi, ki, wi, Q, K, V, k)
     bad = ((out - ref2).abs() > 1e-3 + rtol * ref2.abs()).any(-1).any(-1)
     assert bad.float().mean() < 0.002, "rows differing from the independent oracle"
+    if tc_out is not None:
+        assert (tc_out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
 
 
 def test_row_sharded_forward_equals_whole(cuda):
@@ -144,6 +164,7 @@ def test_fused_small_matches_three_stage_pipeline(cuda, B, T, HI, DI, HQ, D, k, 
     from dsa_attention import dsa_forward
     args = [x.to(cuda) for x in o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype)]
     kk = min(k, T)
+    monkeypatch.setenv("DSA_ATTN_GATHER", "1")    # the staged stage 3 in fp32 arithmetic, as fused
     staged = dsa_forward(*args, kk).cpu()
     monkeypatch.setenv("DSA_FUSED_SMALL", "1")
     fused = dsa_forward(*args, kk).cpu()

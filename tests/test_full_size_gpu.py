@@ -6,6 +6,7 @@ are checked against the oracle:
   - top-K on every row: the count of scores strictly above the threshold is
     < k, the count at or above it is >= min(k, t+1); the kept list is
     ascending, in 0..t, and holds exactly the positions >= threshold;
+  - the kept-set bitmap of every row holds exactly cnt bits;
   - sampled rows: threshold and kept list bit-exact against the C oracle on
     the GPU's score row; indexer scores within the bf16 tolerance of the
     fp32 oracle; attention output within tolerance of the oracle run on the
@@ -37,7 +38,8 @@ def _inputs(cfg, dev):
 
 @pytest.mark.parametrize("name", ["c4", "c5"])
 def test_forward_full_size(cuda, name):
-    from dsa_attention import dsa_forward, sparse_attention_with_lists
+    import _native
+    from dsa_attention import dsa_forward, kept_bitmap, sparse_attention_with_bitmap, sparse_attention_with_lists
     from lightning_indexer import indexer_scores
     from topk import idx_cap_for, topk_select
     cfg = CONFIGS[name]
@@ -49,7 +51,11 @@ def test_forward_full_size(cuda, name):
     sc = indexer_scores(*args[:3], fill_upper=False)
     cap = idx_cap_for(k, T)
     thr, idx, cnt = topk_select(sc, k, causal=True, idx_cap=cap)
-    O2 = sparse_attention_with_lists(idx, cnt, cap, sc, thr, *args[3:])
+    if _native.attn_tc_supported(args[3], args[5]):
+        # bf16 heads of 64/128: dsa_forward's stage 3 is the tensor-core kernel over the bitmap
+        O2 = sparse_attention_with_bitmap(kept_bitmap(sc, thr), *args[3:])
+    else:
+        O2 = sparse_attention_with_lists(idx, cnt, cap, sc, thr, *args[3:])
     assert torch.equal(O, O2), "dsa_forward differs from its own stages"
     assert torch.isfinite(O).all()
 
@@ -69,6 +75,11 @@ def test_forward_full_size(cuda, name):
     assert bool((above < k).all())
     assert bool((atleast >= torch.clamp(t + 1, max=k)).all())
     assert torch.equal(atleast, cnt.long())
+    bits = kept_bitmap(sc, thr)
+    pop = torch.zeros(rows, device=cuda, dtype=torch.int64)
+    for sh in range(32):                                 # popcount, one bit position at a time
+        pop += ((bits >> sh) & 1).sum(1)
+    assert torch.equal(pop, cnt.long())
     n = torch.clamp(cnt.long(), max=cap)
     valid = torch.arange(cap, device=cuda).unsqueeze(0) < n.unsqueeze(1)
     il = idx.long()
