@@ -402,6 +402,372 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Two query tiles per work unit, ping-pong (the default kernel).
+//
+// A unit is (batch, head, query tiles 2m and 2m+1).  Both tiles are computed
+// against the same K/V blocks, so every K/V block is loaded once for 256
+// query rows, and two softmax warpgroups alternate on the tensor core: while
+// warpgroup A turns S_A(j) into P_A(j), the MMA warp runs PV_B(j-1) and
+// S_B(j), and the other way round.  Issue order of the MMA warp per key
+// block j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).
+//   warps 0..3   warp 0 TMA producer, warp 1 MMA issuer, warps 2-3 idle;
+//                this warpgroup lowers its registers to 72 (setmaxnreg)
+//   warps 4..7   softmax of tile A, warps 8..11 softmax of tile B; each
+//                raises its registers to 216 and keeps its row of S_j (128
+//                fp32 values) in registers
+// TMEM (512 columns): S_A 0..127, O_A 128.., S_B 256..383, O_B 384..
+// The launch needs 384 x 168 registers (the pool the two setmaxnreg steps
+// redistribute: 128 x 72 + 256 x 216 = 384 x 168); the host checks the
+// compiled register count before choosing this kernel.
+constexpr int NT2 = 384;
+constexpr uint32_t REG_LOW = 72, REG_HIGH = 216;
+constexpr uint32_t REG_LAUNCH = 168;   // registers per thread the launch must have
+static_assert(128 * REG_LOW + 256 * REG_HIGH == NT2 * REG_LAUNCH,
+              "the setmaxnreg split must add up to the launch's register pool");
+
+struct Unit2 {
+    int b, h, qa, na, nb;   // tile A = qa, tile B = qa + 1 (nb = 0: no tile B)
+};
+
+__device__ __forceinline__ int tile_blocks(int qt, const AtParams& p) {
+    int64_t tq_end = (int64_t)(qt + 1) * BM;
+    if (tq_end > p.T_q) tq_end = p.T_q;
+    int64_t nb = (p.q_row0 + tq_end - 1) / BN + 1;
+    if (nb > p.nkb) nb = p.nkb;
+    return (int)nb;
+}
+
+// unit index -> (batch, head, tile pair); the pairs with the most key blocks first
+__device__ __forceinline__ Unit2 decode_unit2(int u, const AtParams& p) {
+    Unit2 r;
+    const int bh = p.B * p.HQ;
+    const int npair = (p.n_qt + 1) >> 1;
+    const int qr = u / bh, rem = u - qr * bh;
+    const int m = npair - 1 - qr;
+    r.b = rem / p.HQ;
+    r.h = rem - r.b * p.HQ;
+    r.qa = 2 * m;
+    r.na = tile_blocks(r.qa, p);
+    r.nb = r.qa + 1 < p.n_qt ? tile_blocks(r.qa + 1, p) : 0;
+    return r;
+}
+
+template <bool F16>
+__global__ void __launch_bounds__(NT2, 1)
+    attn_tc2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                    const __grid_constant__ CUtensorMap tmv, const AtParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int s_abort;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    // Q_A Q_B | K ring | V ring | P_A P_B | barriers (V is followed by P)
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + 2 * (size_t)p.q_bytes;
+    uint8_t* sV = sK + (size_t)p.nK * p.kv_bytes;
+    uint8_t* sP = sV + (size_t)p.nV * p.kv_bytes;
+    uint64_t* q_full = reinterpret_cast<uint64_t*>(sP + 2 * (size_t)PBYTES);
+    uint64_t* q_empty = q_full + 1;
+    uint64_t* k_full = q_empty + 1;
+    uint64_t* k_empty = k_full + p.nK;
+    uint64_t* v_full = k_empty + p.nK;
+    uint64_t* v_empty = v_full + p.nV;
+    uint64_t* s_full = v_empty + p.nV;   // [2] S_X(j) in TMEM
+    uint64_t* p_full = s_full + 2;       // [2] P_X(j) in shared memory (S_X's columns read)
+    uint64_t* pv_done = p_full + 2;      // [2] O_X += P_X(j) V(j) done
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = p.D / 64;
+    int* flag = &g_attn_tc_timeout;
+
+    if (threadIdx.x == 32) {
+        s_abort = 0;
+        mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        for (int s = 0; s < p.nK; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < p.nV; ++s) {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&s_full[s], 1);
+            mbar_init(&p_full[s], 4);
+            mbar_init(&pv_done[s], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_slot;
+    const int npair = (p.n_qt + 1) >> 1;
+    const int total = npair * p.B * p.HQ;
+
+    if (warp < 4) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_LOW));
+        if (warp == 0 && lane == 0) {
+            // ---------------- TMA producer ----------------
+            int ks = 0, vs = 0;
+            uint32_t kph = 0, vph = 0, qph = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+                const Unit2 w = decode_unit2(u, p);
+                const int nblk = w.nb > w.na ? w.nb : w.na;
+                if (!(ok = mbar_wait(q_empty, qph ^ 1, &s_abort, p.timeout_ns, flag))) break;
+                qph ^= 1;
+                if (!p.stall) {
+                    mbar_expect_tx(q_full, p.q_bytes * (w.nb ? 2u : 1u));
+                    for (int x = 0; x < (w.nb ? 2 : 1); ++x)
+                        for (int c = 0; c < nch; ++c)
+                            tma_load_4d(sQ + (size_t)x * p.q_bytes + c * BM * 128, &tmq, q_full, c * 64,
+                                        w.h, (w.qa + x) * BM, w.b);
+                }
+                for (int j = 0; j < nblk; ++j) {
+                    if (!(ok = mbar_wait(&k_empty[ks], kph ^ 1, &s_abort, p.timeout_ns, flag))) break;
+                    if (!p.stall) {
+                        mbar_expect_tx(&k_full[ks], p.kv_bytes);
+                        for (int c = 0; c < nch; ++c)
+                            tma_load_4d(sK + (size_t)ks * p.kv_bytes + c * BN * 128, &tmk, &k_full[ks],
+                                        c * 64, w.h, j * BN, w.b);
+                    }
+                    if (++ks == p.nK) { ks = 0; kph ^= 1; }
+                    if (!(ok = mbar_wait(&v_empty[vs], vph ^ 1, &s_abort, p.timeout_ns, flag))) break;
+                    if (!p.stall) {
+                        mbar_expect_tx(&v_full[vs], p.kv_bytes);
+                        for (int c = 0; c < nch; ++c)
+                            tma_load_4d(sV + (size_t)vs * p.kv_bytes + c * BN * 128, &tmv, &v_full[vs],
+                                        c * 64, w.h, j * BN, w.b);
+                    }
+                    if (++vs == p.nV) { vs = 0; vph ^= 1; }
+                }
+            }
+        } else if (warp == 1 && lane == 0) {
+            // ---------------- MMA issuer ----------------
+            const uint32_t fmt = F16 ? 0u : 1u;
+            const uint32_t idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                     ((uint32_t)(BM >> 4) << 24);
+            const uint32_t idesc_o = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) |
+                                     ((uint32_t)(p.D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+            int ks = 0, vs = 0;
+            uint32_t kph = 0, vph = 0, qph = 0;
+            uint32_t G[2] = {0, 0};   // blocks issued per tile slot
+            bool ok = true;
+            auto issue_s = [&](int x, uint32_t kb) {
+                const uint32_t qb = smem_u32(sQ + (size_t)x * p.q_bytes);
+                const uint32_t d = tmem_base + (uint32_t)x * 256u;
+                for (int c = 0; c < nch; ++c) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma<false>(d, sw128_desc(qb + c * BM * 128 + kk * 32),
+                                    sw128_desc(kb + c * BN * 128 + kk * 32), idesc_s, (c | kk) != 0);
+                }
+                umma_commit(&s_full[x]);
+            };
+            auto issue_pv = [&](int x, uint32_t vb, int j) {
+                const uint32_t pa = smem_u32(sP + (size_t)x * PBYTES);
+                const uint32_t d = tmem_base + (uint32_t)x * 256u + 128u;
+#pragma unroll
+                for (int kb = 0; kb < BN / 16; ++kb)
+                    umma<false>(d, sw128_desc(pa + (kb >> 2) * BM * 128 + (kb & 3) * 32),
+                                sw128_desc_mn(vb + kb * 16 * 128, BN * 128), idesc_o, (j | kb) != 0);
+                umma_commit(&pv_done[x]);
+            };
+            for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+                const Unit2 w = decode_unit2(u, p);
+                const int n[2] = {w.na, w.nb};
+                const int nblk = w.nb > w.na ? w.nb : w.na;
+                if (!(ok = mbar_wait(q_full, qph, &s_abort, p.timeout_ns, flag))) break;
+                qph ^= 1;
+                if (!(ok = mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag))) break;
+                tc_fence_after();
+                {
+                    const uint32_t kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
+#pragma unroll
+                    for (int x = 0; x < 2; ++x)
+                        if (n[x] > 0) issue_s(x, kb);
+                    umma_commit(&k_empty[ks]);
+                    if (++ks == p.nK) { ks = 0; kph ^= 1; }
+                    if (nblk == 1) umma_commit(q_empty);
+                }
+                for (int j = 0; ok && j < nblk; ++j) {
+                    bool have_v = false, have_k = false;
+                    uint32_t kb = 0;
+                    const uint32_t vb = smem_u32(sV + (size_t)vs * p.kv_bytes);
+#pragma unroll
+                    for (int x = 0; x < 2; ++x) {
+                        if (j >= n[x]) continue;
+                        if (!(ok = mbar_wait(&p_full[x], G[x] & 1, &s_abort, p.timeout_ns, flag))) break;
+                        if (!have_v) {
+                            if (!(ok = mbar_wait(&v_full[vs], vph, &s_abort, p.timeout_ns, flag))) break;
+                            have_v = true;
+                        }
+                        tc_fence_after();
+                        issue_pv(x, vb, j);
+                        ++G[x];
+                        if (j + 1 < n[x]) {
+                            if (!have_k) {
+                                if (!(ok = mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag)))
+                                    break;
+                                tc_fence_after();
+                                kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
+                                have_k = true;
+                            }
+                            issue_s(x, kb);
+                        }
+                    }
+                    if (!ok) break;
+                    umma_commit(&v_empty[vs]);
+                    if (++vs == p.nV) { vs = 0; vph ^= 1; }
+                    if (have_k) {
+                        umma_commit(&k_empty[ks]);
+                        if (++ks == p.nK) { ks = 0; kph ^= 1; }
+                        if (j + 2 == nblk) umma_commit(q_empty);   // the unit's last S was issued
+                    }
+                }
+            }
+        }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_HIGH));
+        // ---------------- softmax: warpgroup x = 0 (tile A) or 1 (tile B) ----------------
+        const int x = (warp >> 2) - 1;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        const uint32_t s_col = tmem_base + lane_off + (uint32_t)x * 256u;
+        const uint32_t o_col = s_col + 128u;
+        uint8_t* prow_base = sP + (size_t)x * PBYTES + row * 128;
+        auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
+            const bool r = mbar_wait(b, parity, &s_abort, p.timeout_ns, flag);
+            return __all_sync(0xffffffffu, r);
+        };
+        uint32_t G = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+            const Unit2 w = decode_unit2(u, p);
+            const int nblk = x == 0 ? w.na : w.nb;
+            if (nblk == 0) continue;
+            const int qt = w.qa + x;
+            const int64_t tq = (int64_t)qt * BM + row;
+            const bool row_ok = tq < p.T_q;
+            const uint32_t* brow = p.bits + ((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.words;
+            float m_run = kNegInf, l = 0.f;
+            uint4 mk = row_ok ? __ldg(reinterpret_cast<const uint4*>(brow)) : make_uint4(0, 0, 0, 0);
+            for (int j = 0; j < nblk; ++j, ++G) {
+                if (!(ok = wait_all(&s_full[x], G & 1))) break;
+                tc_fence_after();
+                uint32_t s[128];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, s + c * 32);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_wait_ld32(s + c * 32);
+
+                const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
+                if (row_ok && j + 1 < nblk) mk = __ldg(reinterpret_cast<const uint4*>(brow) + j + 1);
+                float mxp[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mxp[e] = kNegInf;
+#pragma unroll
+                for (int c = 0; c < 128; ++c) {
+                    const float v = ((mw[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(s[c]) : kNegInf;
+                    s[c] = __float_as_uint(v);
+                    mxp[c & 7] = fmaxf(mxp[c & 7], v);
+                }
+                const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+                const float m_new = fmaxf(m_run, mx * p.sl2);
+                const bool need = m_new > m_run + 8.f;
+                float alpha = 1.f;
+                if (need) {
+                    alpha = ex2(m_run - m_new);
+                    m_run = m_new;
+                    l *= alpha;
+                }
+                // P_X's buffer and O_X: PV_X(j-1) must have landed
+                if (j > 0 && !(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
+                const float mu = m_run == kNegInf ? 0.f : m_run;
+                float lp[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) lp[e] = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        float pv[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            pv[e] = ex2(fmaf(__uint_as_float(s[cc * 64 + i * 8 + e]), p.sl2, -mu));
+                            lp[e] += pv[e];
+                        }
+                        uint4 pk;
+                        pk.x = pack2(pv[0], pv[1], F16);
+                        pk.y = pack2(pv[2], pv[3], F16);
+                        pk.z = pack2(pv[4], pv[5], F16);
+                        pk.w = pack2(pv[6], pv[7], F16);
+                        *reinterpret_cast<uint4*>(prow_base + cc * BM * 128 + ((i ^ (row & 7)) << 4)) = pk;
+                    }
+                }
+                l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+                // rescale O_X (after the row's S values are dead); PV_X(j) is
+                // issued only after p_full, so it sees the rescaled O
+                if (j > 0 && __any_sync(0xffffffffu, need)) {
+                    tc_fence_after();
+                    for (int c = 0; c < p.D / 32; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(o_col + c * 32, o);
+                        tmem_wait_ld32(o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st32(o_col + c * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[x]);
+            }
+            if (!ok) break;
+            if (!(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            float* orow = p.O + (((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.HQ + w.h) * p.D;
+            for (int c = 0; c < p.D / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(o_col + c * 32, o);
+                tmem_wait_ld32(o);
+                if (row_ok) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4)
+                        *reinterpret_cast<float4*>(orow + c * 32 + e) =
+                            make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                                        __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+                }
+            }
+            tc_fence_before();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // Kept-set bitmap: bit (s & 31) of word s/32 of query row r is set iff
 // s <= q_row0 + r % T_q and scores[r, s] >= thr[r].  One CTA per query row;
 // each warp turns 32 consecutive scores into one word with a ballot.  Words
@@ -494,28 +860,49 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
     p.timeout_ns = p.stall ? 20000000ull : 2000000000ull;
     if (units == 0) return DSA_OK;
 
-    auto kern = dtype == DSA_F16 ? attn_tc_kernel<true> : attn_tc_kernel<false>;
     int dev = 0, optin = 0;
-    cudaFuncAttributes fa;
     if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
         return fail(DSA_ERR_CUDA, "attn_tc: cannot query shared memory limits");
-    // rings: K and V stages of equal depth (2..4), two P buffers when they fit
-    const size_t avail = (size_t)optin - fa.sharedSizeBytes - 1024 - 256;
-    p.nP = 2;
-    size_t rest = avail - p.q_bytes - 2 * (size_t)PBYTES;
-    int n = (int)(rest / (2 * (size_t)p.kv_bytes));
-    if (n < 2) {
-        p.nP = 1;
-        rest = avail - p.q_bytes - PBYTES;
-        n = (int)(rest / (2 * (size_t)p.kv_bytes));
+    // The two-tile kernel redistributes a launch pool of exactly 384 x 168
+    // registers; it runs only when the compiled kernel asks for that many.
+    auto kern2 = dtype == DSA_F16 ? attn_tc2_kernel<true> : attn_tc2_kernel<false>;
+    auto kern1 = dtype == DSA_F16 ? attn_tc_kernel<true> : attn_tc_kernel<false>;
+    cudaFuncAttributes fa2, fa1;
+    if (cudaFuncGetAttributes(&fa2, kern2) != cudaSuccess || cudaFuncGetAttributes(&fa1, kern1) != cudaSuccess)
+        return fail(DSA_ERR_CUDA, "attn_tc: cannot query kernel attributes");
+    bool two = fa2.numRegs == (int)REG_LAUNCH && !getenv("DSA_ATTN_TC_ONE_TILE");
+    size_t smem = 0;
+    if (two) {
+        // Q_A Q_B, P_A P_B, then as many K and V stages as fit (K first)
+        const size_t avail = (size_t)optin - fa2.sharedSizeBytes - 1024 - 256;
+        const size_t fixed = 2 * (size_t)p.q_bytes + 2 * (size_t)PBYTES;
+        const int n = avail > fixed ? (int)((avail - fixed) / p.kv_bytes) : 0;
+        if (n < 3) {
+            two = false;
+        } else {
+            p.nV = n / 2 > 4 ? 4 : n / 2;
+            p.nK = n - p.nV > 4 ? 4 : n - p.nV;
+            p.nP = 2;
+            smem = 1024 + 256 + fixed + (size_t)(p.nK + p.nV) * p.kv_bytes;
+        }
     }
-    if (n < 2) return -100;
-    if (n > 4) n = 4;
-    p.nK = p.nV = n;
-    const size_t smem = 1024 + 256 + p.q_bytes + (size_t)(p.nK + p.nV) * p.kv_bytes +
-                        (size_t)p.nP * PBYTES;
+    if (!two) {
+        // one tile per unit: K and V stages of equal depth (2..4), two P buffers when they fit
+        const size_t avail = (size_t)optin - fa1.sharedSizeBytes - 1024 - 256;
+        p.nP = 2;
+        size_t rest = avail - p.q_bytes - 2 * (size_t)PBYTES;
+        int n = (int)(rest / (2 * (size_t)p.kv_bytes));
+        if (n < 2) {
+            p.nP = 1;
+            rest = avail - p.q_bytes - PBYTES;
+            n = (int)(rest / (2 * (size_t)p.kv_bytes));
+        }
+        if (n < 2) return -100;
+        if (n > 4) n = 4;
+        p.nK = p.nV = n;
+        smem = 1024 + 256 + p.q_bytes + (size_t)(p.nK + p.nV) * p.kv_bytes + (size_t)p.nP * PBYTES;
+    }
 
     const CUtensorMapDataType dt = dtype == DSA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -537,12 +924,14 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
         rc = encode_map(&tmv, V, 4, dims, str, box, "attn_tc: V", dt);
         if (rc) return rc;
     }
+    auto kern = two ? kern2 : kern1;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return fail(DSA_ERR_CUDA, "attn_tc: cannot set dynamic shared memory size");
+    const int64_t work = two ? (int64_t)((p.n_qt + 1) / 2) * B * HQ : p.total_units;
     int grid = num_sms();
-    if (grid > p.total_units) grid = p.total_units;
-    kern<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, tmv, p);
-    return check_launch("attn_tc_kernel");
+    if (grid > work) grid = (int)work;
+    kern<<<grid, two ? NT2 : NTHREADS, smem, stream>>>(tmq, tmk, tmv, p);
+    return check_launch(two ? "attn_tc2_kernel" : "attn_tc_kernel");
 }
 
 }  // namespace dsa
