@@ -407,10 +407,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 //
 // A unit is (batch, head, query tiles 2m and 2m+1).  Both tiles are computed
 // against the same K/V blocks, so every K/V block is loaded once for 256
-// query rows, and two softmax warpgroups alternate on the tensor core: while
-// warpgroup A turns S_A(j) into P_A(j), the MMA warp runs PV_B(j-1) and
-// S_B(j), and the other way round.  Issue order of the MMA warp per key
-// block j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).
+// query rows, and two softmax warpgroups share the tensor core.  A softmax
+// warpgroup frees its S columns as soon as it has read S_X(j) into registers
+// (P goes to shared memory), so S_X(j+1) is computed while it still works on
+// block j.  Issue order of the MMA warp: S_A(j), S_B(j), PV_A(j-1), PV_B(j-1).
 //   warps 0..3   warp 0 TMA producer, warp 1 MMA issuer, warps 2-3 idle;
 //                this warpgroup lowers its registers to 72 (setmaxnreg)
 //   warps 4..7   softmax of tile A, warps 8..11 softmax of tile B; each
@@ -474,7 +474,8 @@ __global__ void __launch_bounds__(NT2, 1)
     uint64_t* v_full = k_empty + p.nK;
     uint64_t* v_empty = v_full + p.nV;
     uint64_t* s_full = v_empty + p.nV;   // [2] S_X(j) in TMEM
-    uint64_t* p_full = s_full + 2;       // [2] P_X(j) in shared memory (S_X's columns read)
+    uint64_t* s_free = s_full + 2;       // [2] softmax X has read S_X(j) into registers
+    uint64_t* p_full = s_free + 2;       // [2] P_X(j) in shared memory
     uint64_t* pv_done = p_full + 2;      // [2] O_X += P_X(j) V(j) done
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -495,6 +496,7 @@ __global__ void __launch_bounds__(NT2, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&s_full[s], 1);
+            mbar_init(&s_free[s], 4);
             mbar_init(&p_full[s], 4);
             mbar_init(&pv_done[s], 1);
         }
@@ -533,15 +535,21 @@ __global__ void __launch_bounds__(NT2, 1)
                             tma_load_4d(sQ + (size_t)x * p.q_bytes + c * BM * 128, &tmq, q_full, c * 64,
                                         w.h, (w.qa + x) * BM, w.b);
                 }
-                for (int j = 0; j < nblk; ++j) {
-                    if (!(ok = mbar_wait(&k_empty[ks], kph ^ 1, &s_abort, p.timeout_ns, flag))) break;
+                // K runs one block ahead of V: the MMA needs K(j+1) before V(j)
+                auto load_k = [&](int jb) -> bool {
+                    if (!mbar_wait(&k_empty[ks], kph ^ 1, &s_abort, p.timeout_ns, flag)) return false;
                     if (!p.stall) {
                         mbar_expect_tx(&k_full[ks], p.kv_bytes);
                         for (int c = 0; c < nch; ++c)
                             tma_load_4d(sK + (size_t)ks * p.kv_bytes + c * BN * 128, &tmk, &k_full[ks],
-                                        c * 64, w.h, j * BN, w.b);
+                                        c * 64, w.h, jb * BN, w.b);
                     }
                     if (++ks == p.nK) { ks = 0; kph ^= 1; }
+                    return true;
+                };
+                if (!(ok = load_k(0))) break;
+                for (int j = 0; j < nblk; ++j) {
+                    if (j + 1 < nblk && !(ok = load_k(j + 1))) break;
                     if (!(ok = mbar_wait(&v_empty[vs], vph ^ 1, &s_abort, p.timeout_ns, flag))) break;
                     if (!p.stall) {
                         mbar_expect_tx(&v_full[vs], p.kv_bytes);
@@ -561,9 +569,14 @@ __global__ void __launch_bounds__(NT2, 1)
                                      ((uint32_t)(p.D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
             int ks = 0, vs = 0;
             uint32_t kph = 0, vph = 0, qph = 0;
-            uint32_t G[2] = {0, 0};   // blocks issued per tile slot
+            uint32_t GS[2] = {0, 0}, GP[2] = {0, 0};   // S and PV issued per tile slot
             bool ok = true;
-            auto issue_s = [&](int x, uint32_t kb) {
+            // S_X = Q_X K^T once softmax X has read its previous S out of TMEM
+            auto issue_s = [&](int x, uint32_t kb) -> bool {
+                if (GS[x] > 0 &&
+                    !mbar_wait(&s_free[x], (GS[x] - 1) & 1, &s_abort, p.timeout_ns, flag))
+                    return false;
+                tc_fence_after();
                 const uint32_t qb = smem_u32(sQ + (size_t)x * p.q_bytes);
                 const uint32_t d = tmem_base + (uint32_t)x * 256u;
                 for (int c = 0; c < nch; ++c) {
@@ -573,8 +586,13 @@ __global__ void __launch_bounds__(NT2, 1)
                                     sw128_desc(kb + c * BN * 128 + kk * 32), idesc_s, (c | kk) != 0);
                 }
                 umma_commit(&s_full[x]);
+                ++GS[x];
+                return true;
             };
-            auto issue_pv = [&](int x, uint32_t vb, int j) {
+            // O_X (+)= P_X V once softmax X has written P_X
+            auto issue_pv = [&](int x, uint32_t vb, int j) -> bool {
+                if (!mbar_wait(&p_full[x], GP[x] & 1, &s_abort, p.timeout_ns, flag)) return false;
+                tc_fence_after();
                 const uint32_t pa = smem_u32(sP + (size_t)x * PBYTES);
                 const uint32_t d = tmem_base + (uint32_t)x * 256u + 128u;
 #pragma unroll
@@ -582,6 +600,8 @@ __global__ void __launch_bounds__(NT2, 1)
                     umma<false>(d, sw128_desc(pa + (kb >> 2) * BM * 128 + (kb & 3) * 32),
                                 sw128_desc_mn(vb + kb * 16 * 128, BN * 128), idesc_o, (j | kb) != 0);
                 umma_commit(&pv_done[x]);
+                ++GP[x];
+                return true;
             };
             for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
                 const Unit2 w = decode_unit2(u, p);
@@ -589,50 +609,28 @@ __global__ void __launch_bounds__(NT2, 1)
                 const int nblk = w.nb > w.na ? w.nb : w.na;
                 if (!(ok = mbar_wait(q_full, qph, &s_abort, p.timeout_ns, flag))) break;
                 qph ^= 1;
-                if (!(ok = mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag))) break;
-                tc_fence_after();
-                {
-                    const uint32_t kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
+                // per key block j: S_A(j), S_B(j), then PV_A(j-1), PV_B(j-1)
+                for (int j = 0; ok && j <= nblk; ++j) {
+                    if (j < nblk) {
+                        if (!(ok = mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag))) break;
+                        const uint32_t kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
 #pragma unroll
-                    for (int x = 0; x < 2; ++x)
-                        if (n[x] > 0) issue_s(x, kb);
-                    umma_commit(&k_empty[ks]);
-                    if (++ks == p.nK) { ks = 0; kph ^= 1; }
-                    if (nblk == 1) umma_commit(q_empty);
-                }
-                for (int j = 0; ok && j < nblk; ++j) {
-                    bool have_v = false, have_k = false;
-                    uint32_t kb = 0;
-                    const uint32_t vb = smem_u32(sV + (size_t)vs * p.kv_bytes);
-#pragma unroll
-                    for (int x = 0; x < 2; ++x) {
-                        if (j >= n[x]) continue;
-                        if (!(ok = mbar_wait(&p_full[x], G[x] & 1, &s_abort, p.timeout_ns, flag))) break;
-                        if (!have_v) {
-                            if (!(ok = mbar_wait(&v_full[vs], vph, &s_abort, p.timeout_ns, flag))) break;
-                            have_v = true;
-                        }
-                        tc_fence_after();
-                        issue_pv(x, vb, j);
-                        ++G[x];
-                        if (j + 1 < n[x]) {
-                            if (!have_k) {
-                                if (!(ok = mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag)))
-                                    break;
-                                tc_fence_after();
-                                kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
-                                have_k = true;
-                            }
-                            issue_s(x, kb);
-                        }
-                    }
-                    if (!ok) break;
-                    umma_commit(&v_empty[vs]);
-                    if (++vs == p.nV) { vs = 0; vph ^= 1; }
-                    if (have_k) {
+                        for (int x = 0; x < 2; ++x)
+                            if (j < n[x] && !(ok = issue_s(x, kb))) break;
+                        if (!ok) break;
                         umma_commit(&k_empty[ks]);
                         if (++ks == p.nK) { ks = 0; kph ^= 1; }
-                        if (j + 2 == nblk) umma_commit(q_empty);   // the unit's last S was issued
+                        if (j + 1 == nblk) umma_commit(q_empty);   // the unit's last S was issued
+                    }
+                    if (j > 0) {
+                        if (!(ok = mbar_wait(&v_full[vs], vph, &s_abort, p.timeout_ns, flag))) break;
+                        const uint32_t vb = smem_u32(sV + (size_t)vs * p.kv_bytes);
+#pragma unroll
+                        for (int x = 0; x < 2; ++x)
+                            if (j - 1 < n[x] && !(ok = issue_pv(x, vb, j - 1))) break;
+                        if (!ok) break;
+                        umma_commit(&v_empty[vs]);
+                        if (++vs == p.nV) { vs = 0; vph ^= 1; }
                     }
                 }
             }
@@ -671,20 +669,27 @@ __global__ void __launch_bounds__(NT2, 1)
                 for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, s + c * 32);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) tmem_wait_ld32(s + c * 32);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[x]);   // the MMA may write S_X(j+1)
 
                 const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
                 if (row_ok && j + 1 < nblk) mk = __ldg(reinterpret_cast<const uint4*>(brow) + j + 1);
+                // dropped logits -> -inf; row max of the kept ones (8 chains of 3-input max)
                 float mxp[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) mxp[e] = kNegInf;
 #pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const float v = ((mw[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(s[c]) : kNegInf;
-                    s[c] = __float_as_uint(v);
-                    mxp[c & 7] = fmaxf(mxp[c & 7], v);
+                for (int c = 0; c < 128; c += 2) {
+                    const float v0 = ((mw[c >> 5] >> (c & 31)) & 1u) ? __uint_as_float(s[c]) : kNegInf;
+                    const float v1 =
+                        ((mw[c >> 5] >> ((c + 1) & 31)) & 1u) ? __uint_as_float(s[c + 1]) : kNegInf;
+                    s[c] = __float_as_uint(v0);
+                    s[c + 1] = __float_as_uint(v1);
+                    mxp[(c >> 1) & 7] = fmax3(mxp[(c >> 1) & 7], v0, v1);
                 }
-                const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+                const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                                       fmaxf(mxp[6], mxp[7]));
                 const float m_new = fmaxf(m_run, mx * p.sl2);
                 const bool need = m_new > m_run + 8.f;
                 float alpha = 1.f;
@@ -695,7 +700,12 @@ __global__ void __launch_bounds__(NT2, 1)
                 }
                 // P_X's buffer and O_X: PV_X(j-1) must have landed
                 if (j > 0 && !(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
+                // P = 2^(x*sl2 - m): the exponent in fp32 (packed FMA), rounded to the
+                // 16-bit input type, two exponentials per MUFU op; l sums the
+                // rounded P values that the PV product consumes.  16-byte slot i
+                // of the 128-byte swizzled row holds keys 64*cc + 8*i .. +7.
                 const float mu = m_run == kNegInf ? 0.f : m_run;
+                const float2 sl2v = make_float2(p.sl2, p.sl2), nmu = make_float2(-mu, -mu);
                 float lp[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) lp[e] = 0.f;
@@ -703,18 +713,17 @@ __global__ void __launch_bounds__(NT2, 1)
                 for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        float pv[8];
+                        uint32_t pk[4];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            pv[e] = ex2(fmaf(__uint_as_float(s[cc * 64 + i * 8 + e]), p.sl2, -mu));
-                            lp[e] += pv[e];
+                        for (int e = 0; e < 4; ++e) {
+                            const int c = cc * 64 + i * 8 + 2 * e;
+                            const float2 xx =
+                                fma2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2v, nmu);
+                            pk[e] = ex2_pair<F16>(xx.x, xx.y);
+                            add_pair<F16>(lp[2 * e], lp[2 * e + 1], pk[e]);
                         }
-                        uint4 pk;
-                        pk.x = pack2(pv[0], pv[1], F16);
-                        pk.y = pack2(pv[2], pv[3], F16);
-                        pk.z = pack2(pv[4], pv[5], F16);
-                        pk.w = pack2(pv[6], pv[7], F16);
-                        *reinterpret_cast<uint4*>(prow_base + cc * BM * 128 + ((i ^ (row & 7)) << 4)) = pk;
+                        *reinterpret_cast<uint4*>(prow_base + cc * BM * 128 + ((i ^ (row & 7)) << 4)) =
+                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     }
                 }
                 l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));

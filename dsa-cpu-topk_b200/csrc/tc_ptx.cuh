@@ -209,6 +209,51 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 
+// max(a, b, c) in one instruction
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// (a.x*b.x + c.x, a.y*b.y + c.y), one packed instruction
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+          "l"(*reinterpret_cast<uint64_t*>(&c)));
+    return *reinterpret_cast<float2*>(&d);
+}
+// 2^x of two values rounded to a 16-bit pair (lo = x0, hi = x1): bf16x2
+// (flushes denormal results) or f16x2, on the MUFU, two results per op
+template <bool F16>
+__device__ __forceinline__ uint32_t ex2_pair(float x0, float x1) {
+    uint32_t h, y;
+    if constexpr (F16) {
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+        asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(h));
+    } else {
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+        asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(h));
+    }
+    return y;
+}
+// a0 += lo(v), a1 += hi(v): the two 16-bit values of v widened to fp32
+template <bool F16>
+__device__ __forceinline__ void add_pair(float& a0, float& a1, uint32_t v) {
+    if constexpr (F16) {
+        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+            "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "r"(v));
+    } else {
+        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+            "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "r"(v));
+    }
+}
+
 // ---- host: tensor maps -------------------------------------------------------
 // cuTensorMapEncodeTiled is looked up through the runtime, so the library
 // does not link libcuda (it loads on hosts without a driver).
