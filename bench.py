@@ -444,7 +444,7 @@ def run_b200(args, cfg, world, rank, local):
         stages["topk"]["kernel"] = "topk_cached_kernel (threshold + kept-set bitmap)"
         stages["sparse_attn"] = dict(
             bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_sust,
-            unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc_kernel", traffic=traffic.get("sparse_attn"),
+            unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc2_kernel", traffic=traffic.get("sparse_attn"),
             note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs")
     for v in stages.values():
         v["frac"] = v["achieved"] / v["peak"]
