@@ -357,6 +357,7 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
     __shared__ uint32_t seg_base[NW + 1];
     __shared__ uint32_t res[2];
     __shared__ uint32_t n_cand;
+    __shared__ uint32_t n_keep;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
@@ -441,6 +442,98 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
         const int gs0 = warp * gseg;
         const int gs1 = gs0 + gseg < g4 ? gs0 + gseg : g4;
         uint32_t prefix = d0 << S0, pmask = ~0u << S0;
+
+        if (a.bits && !a.idx && use_cand) {
+            // Bitmap-only rows: one sweep writes every word from the first
+            // digit alone (keys in bins above d0 are kept, below d0 dropped)
+            // and collects bin d0's keys; the exact threshold inside d0 then
+            // ORs the kept candidates in.  k - krem keys lie above bin d0.
+            uint32_t* out = a.bits + row * a.words;
+            // causal groups: keys at or above bin d0+1 set their bit; keys of
+            // bin d0 become candidates (an unordered list: the selection does
+            // not depend on their order).  Only the last group has positions
+            // past `valid`; padding keys are 0, below every real bin above d0.
+            // bin d0 = [lo, hi_key); for the top bin, hi_key = the largest key,
+            // which is kept whatever the threshold in that bin is
+            const uint32_t lo = d0 << S0;
+            const uint32_t hi_key = d0 == NB_TOP - 1 ? 0xffffffffu : (d0 + 1) << S0;
+            const int gw = ((g4 + 7) >> 3) << 3;   // groups of the words holding causal keys
+            constexpr int PIPE = CACHED ? 1 : 4;
+            // loop and break tests use the warp's first group (g0 - lane), so
+            // whole warps run the shuffles; gw is a multiple of 8, so the 8
+            // lanes of a word are all inside or all past it
+            for (int g0 = tid; g0 - lane < gw; g0 += PIPE * BLOCK) {
+                uint4 kb[PIPE];
+#pragma unroll
+                for (int u = 0; u < PIPE; ++u) {
+                    const int g = g0 + u * BLOCK;
+                    kb[u] = g < g4 ? group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < PIPE; ++u) {
+                    const int g = g0 + u * BLOCK;
+                    if (g - lane >= gw) break;
+                    const uint32_t e[4] = {kb[u].x, kb[u].y, kb[u].z, kb[u].w};
+                    uint32_t nib = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) nib |= (uint32_t)(e[j] >= hi_key) << j;
+                    uint32_t wd = nib << (4 * (lane & 7));
+                    wd |= __shfl_xor_sync(0xffffffffu, wd, 1);
+                    wd |= __shfl_xor_sync(0xffffffffu, wd, 2);
+                    wd |= __shfl_xor_sync(0xffffffffu, wd, 4);
+                    if ((lane & 7) == 0 && g < gw) out[g >> 3] = wd;
+                    if (g < g4) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (e[j] - lo < (1u << S0) && (g + 1 < g4 || 4 * g + j < valid)) {
+                                const uint32_t at = atomicAdd(&n_cand, 1u);
+                                cand_key[at] = e[j];
+                                cand_pos[at] = 4 * g + j;
+                            }
+                    }
+                }
+            }
+            // words past the causal end
+            for (int wi = (gw >> 3) + tid; wi < (int)a.words; wi += BLOCK) out[wi] = 0u;
+            if (tid == 0) n_keep = 0;
+            __syncthreads();
+            const int nc = (int)n_cand;
+            const uint32_t above = (uint32_t)a.k - krem;
+#pragma unroll 1
+            for (int pass = 1; pass <= 2; ++pass) {
+                const int shift = pass == 1 ? 10 : 0;
+                const int nb = pass == 1 ? 2048 : 1024;
+                for (int i = tid; i < nb; i += BLOCK) hist[i] = 0;
+                __syncthreads();
+                for (int i = tid; i < nc; i += BLOCK) {
+                    const uint32_t key = cand_key[i];
+                    if ((key & pmask) == prefix)
+                        atomicAdd(&hist[(nb - 1) - ((key >> shift) & (nb - 1))], 1u);
+                }
+                __syncthreads();
+                block_find_desc<BLOCK>(hist, nb, krem, wtot, res);
+                prefix |= res[0] << shift;
+                pmask |= (uint32_t)(nb - 1) << shift;
+                krem = res[1];
+            }
+            // the words are written (the barriers above order them before the ORs)
+            uint32_t kc = 0;
+            for (int i = tid; i < nc; i += BLOCK)
+                if (cand_key[i] >= prefix) {
+                    atomicOr(out + (cand_pos[i] >> 5), 1u << (cand_pos[i] & 31));
+                    ++kc;
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) kc += __shfl_xor_sync(0xffffffffu, kc, o);
+            if (lane == 0 && kc) atomicAdd(&n_keep, kc);
+            __syncthreads();
+            if (tid == 0) {
+                a.thr[row] = key2f(prefix);
+                if (a.cnt) a.cnt[row] = (int32_t)(above + n_keep);
+            }
+            __syncthreads();
+            continue;
+        }
 
         if (use_cand) {
             // ---- sweep 2: candidates + per-segment count of keys above bin d0

@@ -150,6 +150,7 @@ def test_attention_wait_timeout_is_reported_and_recoverable(cuda, monkeypatch):
     (2, 40, 9000, 64, 8960, True),
     (1, 300, 300, 20, 0, True),         # short rows: top-K kernel, then the bitmap kernel
     (3, 5, 5000, 100, 0, False),        # full rows, no causal limit
+    (1, 48, 7000, 3000, 6952, True),    # a third of the scores -inf: thresholds fall in the -inf bin
 ])
 def test_topk_bitmap_equals_threshold_then_bitmap(cuda, B, T_q, T_k, k, q_row0, causal):
     from dsa_attention import kept_bitmap
@@ -157,6 +158,8 @@ def test_topk_bitmap_equals_threshold_then_bitmap(cuda, B, T_q, T_k, k, q_row0, 
     g = torch.Generator(device=cuda).manual_seed(T_k)
     sc = torch.randn(B, T_q, T_k, generator=g, device=cuda)
     sc[:, ::2] = (sc[:, ::2] * 8).round() / 8            # ties at the threshold
+    if k >= 3000:
+        sc[..., ::3] = -math.inf
     thr, cnt, bits = topk_select_bitmap(sc, k, causal=causal, q_row0=q_row0)
     thr2, _, cnt2 = topk_select(sc, k, causal=causal, q_row0=q_row0, idx_cap=32)
     assert torch.equal(thr, thr2) and torch.equal(cnt, cnt2)
@@ -165,3 +168,26 @@ def test_topk_bitmap_equals_threshold_then_bitmap(cuda, B, T_q, T_k, k, q_row0, 
     else:
         ref = torch.from_numpy(_bits_ref(sc.cpu(), thr.cpu(), T_k, bits.shape[1])).to(cuda)
     assert torch.equal(bits, ref)
+
+
+@pytest.mark.parametrize("k", [5, 700, 2000, 4999])
+def test_topk_bitmap_special_values(cuda, k):
+    """+inf, -inf and both signs of zero at the threshold (+0 and -0 tie),
+    on 5000-entry rows, which take the one-sweep bitmap path of the top-K
+    kernel; the result must equal the list-mode selection."""
+    from dsa_attention import kept_bitmap
+    from topk import topk_select, topk_select_bitmap
+    g = torch.Generator(device=cuda).manual_seed(k)
+    sc = torch.randn(2, 3, 5000, generator=g, device=cuda).round()   # many exact ties, zeros of both signs
+    sc[0, 0, ::7] = math.inf
+    sc[0, 1, ::3] = -math.inf
+    sc[1, :, ::2] = -0.0
+    sc[1, 2] = 0.0
+    sc[1, 2, ::5] = -0.0
+    thr, cnt, bits = topk_select_bitmap(sc, k, causal=False)
+    thr2, _, cnt2 = topk_select(sc, k, causal=False, idx_cap=32)
+    assert torch.equal(thr, thr2) and torch.equal(cnt, cnt2)
+    ref = torch.from_numpy(_bits_ref(sc.cpu(), thr.cpu(), 5000, bits.shape[1])).to(cuda)
+    assert torch.equal(bits, ref)
+    pop = sum(((bits >> b) & 1).sum(1) for b in range(32))
+    assert torch.equal(pop, cnt.long())
