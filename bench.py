@@ -52,6 +52,9 @@ CONFIGS = {
     # c5's head shapes at T=8192 (~2 GB on the device): the small case the ncu captures use
     "c5_t8k": dict(B=1, T=8192, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16",
                    desc="c5 head shapes at T8192 (profiling case), bf16, causal"),
+    # rows longer than 8K, as at c5 (the top-K kernel's uncached variant), ~2.5 GB on the device
+    "c5_t16k": dict(B=1, T=16384, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16",
+                    desc="c5 head shapes at T16384 (profiling case), bf16, causal"),
 }
 DT = {"f32": torch.float32, "bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}
 C2 = dict(B=64, T=2048, k=128, desc="top-K only: fp32 scores 64 x 2048 x 2048, N(0,1), s > t = -inf, k=128")
@@ -312,7 +315,7 @@ def cpu_sample_text(ctx, cfg, rows, el):
             f"OMP/torch threads={ctx['threads']}")
 
 
-CHUNK = {"c1": 512, "c3_b64_k128": 512, "c4": 64, "c5": 16, "c5_t8k": 32}
+CHUNK = {"c1": 512, "c3_b64_k128": 512, "c4": 64, "c5": 16, "c5_t8k": 32, "c5_t16k": 32}
 
 
 # --------------------------------------------------------------------------

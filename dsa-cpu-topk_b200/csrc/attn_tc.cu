@@ -34,6 +34,7 @@
 // dsa_device_status().
 #include <cuda.h>
 #include <math.h>
+#include <stdio.h>
 #include <stdlib.h>
 
 #include "common.cuh"
@@ -892,6 +893,14 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
         } else {
             p.nV = n / 2 > 4 ? 4 : n / 2;
             p.nK = n - p.nV > 4 ? 4 : n - p.nV;
+            // DSA_ATTN_KV=<nK>,<nV>: ring depths for tuning (each >= 1, sum <= n)
+            if (const char* kv = getenv("DSA_ATTN_KV")) {
+                int a = 0, b = 0;
+                if (sscanf(kv, "%d,%d", &a, &b) == 2 && a >= 1 && b >= 1 && a + b <= n && a <= 4 && b <= 4) {
+                    p.nK = a;
+                    p.nV = b;
+                }
+            }
             p.nP = 2;
             smem = 1024 + 256 + fixed + (size_t)(p.nK + p.nV) * p.kv_bytes;
         }
