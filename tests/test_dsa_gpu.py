@@ -174,3 +174,33 @@ def test_fused_small_matches_three_stage_pipeline(cuda, B, T, HI, DI, HQ, D, k, 
         ref = o.dsa_attention(*[x.cpu() for x in args], k)
         bad = ((fused - ref).abs() > 1e-3 + 1e-3 * ref.abs()).any(-1).any(-1)
         assert bad.float().mean() < 0.002
+
+
+@pytest.mark.parametrize("B,T,HI,DI,HQ,D,k,dtype", [
+    (16, 512, 4, 32, 4, 32, 32, torch.float32),      # config c1: gather stage 3
+    (1, 1024, 8, 128, 4, 128, 64, torch.bfloat16),   # tensor-core indexer and stage 3
+])
+def test_forward_captures_in_a_cuda_graph(cuda, B, T, HI, DI, HQ, D, k, dtype):
+    """The C ABI only enqueues (no sync, no allocation), so a whole forward can
+    be captured once and replayed; the replay equals eager calls bit for bit,
+    also after the inputs change in place."""
+    import _native
+    args = [x.to(cuda).contiguous() for x in o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype)]
+    ws = torch.empty(_native.forward_workspace_bytes(B, T, T, k), device=cuda, dtype=torch.uint8)
+    O = torch.empty(B, T, HQ, D, device=cuda)
+    run = lambda: _native.forward(*args, O, k, ws)
+    run()                                   # first call on the device outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    for seed in (1, 2):
+        new = o.make_inputs(B, T, HI, DI, HQ, D, D, dtype=dtype, seed0=10 * seed)
+        for a, n in zip(args, new):
+            a.copy_(n.to(cuda))
+        g.replay()
+        torch.cuda.synchronize()
+        replayed = O.clone()
+        run()
+        torch.cuda.synchronize()
+        assert torch.equal(replayed, O)
