@@ -1087,7 +1087,9 @@ static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream) {
         return launch_warp_l2(a, stream);
     if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
         if (longest <= 2048) return launch_cached<128, true>(a, longest, stream);
-        if (longest <= 8192) return launch_cached<256, true>(a, longest, stream);
+        // bitmap-only rows of 4K-8K: re-reading from L2 instead of caching the
+        // keys lets about twice as many rows be in flight (c4 top-K 0.61 -> 0.55 ms)
+        if (longest <= 8192 && !(a.bits && !a.idx)) return launch_cached<256, true>(a, longest, stream);
         // longer rows: the sweeps after the first re-read the row from L2, so
         // several CTAs fit on an SM (DSA_TOPK_SMEM_ROWS=1 caches them instead)
         if (getenv("DSA_TOPK_SMEM_ROWS")) return launch_cached<512, true>(a, longest, stream);
