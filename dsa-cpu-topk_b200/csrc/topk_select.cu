@@ -676,10 +676,12 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
     }
 }
 
+// cand_div: the candidate buffer holds longest / cand_div keys (256..4096);
+// a row whose threshold bin has more keys takes the exact path without it
 template <int BLOCK, bool CACHED>
-int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream) {
+int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream, int cand_div = 4) {
     a.cache_elems = CACHED ? (int)((longest + 3) & ~int64_t(3)) : 0;
-    const int64_t cm = longest / 4;
+    const int64_t cm = longest / cand_div;
     a.cand_max = (int)(cm < 256 ? 256 : cm > 4096 ? 4096 : cm);
     const size_t smem = ((size_t)a.cache_elems + 2 * (size_t)a.cand_max) * sizeof(uint32_t);
     auto kern = topk_cached_kernel<BLOCK, CACHED>;
@@ -1087,9 +1089,11 @@ static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream) {
         return launch_warp_l2(a, stream);
     if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
         if (longest <= 2048) return launch_cached<128, true>(a, longest, stream);
-        // bitmap-only rows of 4K-8K: re-reading from L2 instead of caching the
-        // keys lets about twice as many rows be in flight (c4 top-K 0.61 -> 0.55 ms)
+        // bitmap-only rows of 4K-8K: 128-thread CTAs re-reading the row from L2,
+        // with a candidate buffer of longest/8 keys, instead of 256 threads
+        // caching the keys; far more rows are in flight (c4 top-K 0.61 -> 0.47 ms)
         if (longest <= 8192 && !(a.bits && !a.idx)) return launch_cached<256, true>(a, longest, stream);
+        if (longest <= 8192) return launch_cached<128, false>(a, longest, stream, 8);
         // longer rows: the sweeps after the first re-read the row from L2, so
         // several CTAs fit on an SM (DSA_TOPK_SMEM_ROWS=1 caches them instead)
         if (getenv("DSA_TOPK_SMEM_ROWS")) return launch_cached<512, true>(a, longest, stream);

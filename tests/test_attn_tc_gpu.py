@@ -191,3 +191,18 @@ def test_topk_bitmap_special_values(cuda, k):
     assert torch.equal(bits, ref)
     pop = sum(((bits >> b) & 1).sum(1) for b in range(32))
     assert torch.equal(pop, cnt.long())
+
+
+@pytest.mark.parametrize("levels", [3, 40])
+def test_topk_bitmap_threshold_bin_overflow(cuda, levels):
+    """Rows of 4K-8K entries whose threshold bin holds more keys than the
+    candidate buffer (scores drawn from a few values): the kernel takes its
+    exact path without candidates and must still write the same bitmap."""
+    from topk import topk_select, topk_select_bitmap
+    g = torch.Generator(device=cuda).manual_seed(levels)
+    sc = torch.randint(0, levels, (2, 64, 7000), generator=g, device=cuda).float() / levels
+    thr, cnt, bits = topk_select_bitmap(sc, 900, causal=True, q_row0=6936)
+    thr2, _, cnt2 = topk_select(sc, 900, causal=True, q_row0=6936, idx_cap=32)
+    assert torch.equal(thr, thr2) and torch.equal(cnt, cnt2)
+    ref = torch.from_numpy(_bits_ref(sc.cpu(), thr.cpu(), 6936, bits.shape[1])).to(cuda)
+    assert torch.equal(bits, ref)
