@@ -3,8 +3,11 @@
  *
  * Three sm_100a CUDA stages behind plain pointers and sizes:
  *   stage 1  Lightning Indexer scores   I[b,t,s] = sum_j w[b,t,j] * ReLU(<q[b,t,j,:], k[b,s,:]>)
- *   stage 2  per-row top-K threshold (k-th largest) + kept-index list (keep ties)
- *   stage 3  sparse attention over the kept keys (online softmax)
+ *            (tcgen05 tensor cores for bf16 / e4m3 inputs, CUDA cores otherwise)
+ *   stage 2  per-row top-K threshold (k-th largest, ties kept) + the kept set, as an
+ *            ascending index list or as a bitmap
+ *   stage 3  attention over the kept keys: a masked flash attention on tcgen05 over the
+ *            bitmap (bf16/fp16, head size 64 or 128), else a gather with an fp32 online softmax
  *
  * Conventions shared by every entry point
  *   - All pointers are device pointers on the current CUDA device, row-major
