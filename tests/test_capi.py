@@ -44,11 +44,9 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_library_is_built_for_sm100a():
-    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf",
-                          os.path.join(PKG, "libdsa_b200.so")], capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    assert "sm_100a" in out.stdout
+    """build.py compiles every CUDA source for sm_100a only."""
+    import build
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def test_host_validation_errors(lib):
@@ -68,3 +66,28 @@ def test_host_validation_errors(lib):
         _native._check(_native.DSA_ERR_INVALID, "x")
     with pytest.raises(RuntimeError):
         _native._check(_native.DSA_ERR_CUDA, "x")
+
+
+def test_bitmap_entry_points_validate_on_the_host(lib):
+    """Word counts, sizes and dtypes of the bitmap path are checked before any
+    device work (fake non-null pointers are never dereferenced)."""
+    import _native
+    for T, w in [(1, 4), (128, 4), (129, 8), (512, 16), (32768, 1024)]:
+        assert lib.dsa_bitmap_words(T) == w
+    # the forward workspace holds the bitmap beside scores, thresholds and lists
+    assert lib.dsa_forward_workspace_bytes(1, 1024, 1024, 64) >= 1024 * 1024 * 4 + 1024 * 32 * 4
+    fake = ctypes.c_void_p(256)
+    # too few words per row
+    rc = lib.dsa_kept_bitmap(fake, fake, fake, 1, 128, 1024, 0, 8, None)
+    assert rc == _native.DSA_ERR_INVALID and b"words_per_row" in lib.dsa_last_error_string()
+    rc = lib.dsa_topk_select_bitmap(fake, 128, 1024, 128, 0, 1, 16, fake, None, None, 32, None)
+    assert rc == _native.DSA_ERR_INVALID
+    rc = lib.dsa_topk_select_bitmap(fake, 128, 1024, 128, 0, 1, 16, fake, None, fake, 30, None)
+    assert rc == _native.DSA_ERR_INVALID
+    # fp32 attention inputs are not a tensor-core case
+    rc = lib.dsa_sparse_attn_bitmap(fake, 32, fake, fake, fake, fake, 1, 128, 1024, 0, 4, 128, 128,
+                                    ctypes.c_float(0.1), _native.DSA_F32, None)
+    assert rc == _native.DSA_ERR_UNSUPPORTED
+    rc = lib.dsa_sparse_attn_bitmap(None, 32, fake, fake, fake, fake, 1, 128, 1024, 0, 4, 128, 128,
+                                    ctypes.c_float(0.1), _native.DSA_BF16, None)
+    assert rc == _native.DSA_ERR_INVALID
