@@ -206,3 +206,17 @@ def test_topk_bitmap_threshold_bin_overflow(cuda, levels):
     assert torch.equal(thr, thr2) and torch.equal(cnt, cnt2)
     ref = torch.from_numpy(_bits_ref(sc.cpu(), thr.cpu(), 6936, bits.shape[1])).to(cuda)
     assert torch.equal(bits, ref)
+
+
+def test_row_blocks_of_the_tc_forward_equal_the_whole(cuda):
+    """q_row0 offsets on the tensor-core path: query row blocks that do not
+    start on a tile boundary give the rows of the whole forward bit for bit
+    (each row's softmax does not depend on how rows are grouped into tiles)."""
+    from dsa_attention import dsa_forward
+    qi, ki, wi, Q, K, V = (x.to(cuda) for x in o.make_inputs(1, 900, 4, 128, 2, 128, 128,
+                                                            dtype=torch.bfloat16, seed0=21))
+    whole = dsa_forward(qi, ki, wi, Q, K, V, 100)
+    parts = [dsa_forward(qi[:, a:b].contiguous(), ki, wi[:, a:b].contiguous(), Q[:, a:b].contiguous(), K, V,
+                         100, q_row0=a)
+             for a, b in [(0, 77), (77, 400), (400, 900)]]
+    assert torch.equal(torch.cat(parts, 1), whole)
