@@ -485,15 +485,16 @@ __global__ void __launch_bounds__(NT2, 1)
 
     if (threadIdx.x == 32) {
         s_abort = 0;
+        // Q, K and V stages are released by both MMA issuers (one per tile)
         mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
+        mbar_init(q_empty, 2);
         for (int s = 0; s < p.nK; ++s) {
             mbar_init(&k_full[s], 1);
-            mbar_init(&k_empty[s], 1);
+            mbar_init(&k_empty[s], 2);
         }
         for (int s = 0; s < p.nV; ++s) {
             mbar_init(&v_full[s], 1);
-            mbar_init(&v_empty[s], 1);
+            mbar_init(&v_empty[s], 2);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&s_full[s], 1);
@@ -561,78 +562,91 @@ __global__ void __launch_bounds__(NT2, 1)
                     if (++vs == p.nV) { vs = 0; vph ^= 1; }
                 }
             }
-        } else if (warp == 1 && lane == 0) {
-            // ---------------- MMA issuer ----------------
+        } else if ((warp == 1 || warp == 2) && lane == 0) {
+            // ---------------- MMA issuers: warp 1 for tile A, warp 2 for tile B ----------------
+            // Each issuer waits only on its own tile's softmax, so one tile's PV
+            // never queues behind the other tile's progress (tile B usually has
+            // one more key block per unit).  Per key block j of its tile:
+            // S(j+1) once the softmax has read S(j) out of TMEM, then PV(j) once
+            // it has written P(j).  Blocks of the unit that only the other tile
+            // uses are released without an MMA.
+            const int x = warp - 1;
             const uint32_t fmt = F16 ? 0u : 1u;
             const uint32_t idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                                      ((uint32_t)(BM >> 4) << 24);
             const uint32_t idesc_o = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) |
                                      ((uint32_t)(p.D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+            const uint32_t qb = smem_u32(sQ + (size_t)x * p.q_bytes);
+            const uint32_t s_tm = tmem_base + (uint32_t)x * 256u;
+            const uint32_t o_tm = s_tm + 128u;
+            const uint32_t pa = smem_u32(sP + (size_t)x * PBYTES);
             int ks = 0, vs = 0;
-            uint32_t kph = 0, vph = 0, qph = 0;
-            uint32_t GS[2] = {0, 0}, GP[2] = {0, 0};   // S and PV issued per tile slot
+            uint32_t kph = 0, vph = 0, qph = 0, GS = 0, GP = 0;
             bool ok = true;
-            // S_X = Q_X K^T once softmax X has read its previous S out of TMEM
-            auto issue_s = [&](int x, uint32_t kb) -> bool {
-                if (GS[x] > 0 &&
-                    !mbar_wait(&s_free[x], (GS[x] - 1) & 1, &s_abort, p.timeout_ns, flag))
-                    return false;
+            auto k_next = [&]() { if (++ks == p.nK) { ks = 0; kph ^= 1; } };
+            auto v_next = [&]() { if (++vs == p.nV) { vs = 0; vph ^= 1; } };
+            // S = Q K^T into this tile's S columns, K from the current K stage
+            auto issue_s = [&]() -> bool {
+                if (!mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag)) return false;
+                if (GS > 0 && !mbar_wait(&s_free[x], (GS - 1) & 1, &s_abort, p.timeout_ns, flag)) return false;
                 tc_fence_after();
-                const uint32_t qb = smem_u32(sQ + (size_t)x * p.q_bytes);
-                const uint32_t d = tmem_base + (uint32_t)x * 256u;
+                const uint32_t kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
                 for (int c = 0; c < nch; ++c) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        umma<false>(d, sw128_desc(qb + c * BM * 128 + kk * 32),
+                        umma<false>(s_tm, sw128_desc(qb + c * BM * 128 + kk * 32),
                                     sw128_desc(kb + c * BN * 128 + kk * 32), idesc_s, (c | kk) != 0);
                 }
                 umma_commit(&s_full[x]);
-                ++GS[x];
+                umma_commit(&k_empty[ks]);
+                ++GS;
+                k_next();
                 return true;
             };
-            // O_X (+)= P_X V once softmax X has written P_X
-            auto issue_pv = [&](int x, uint32_t vb, int j) -> bool {
-                if (!mbar_wait(&p_full[x], GP[x] & 1, &s_abort, p.timeout_ns, flag)) return false;
+            // O (+)= P V, V from the current V stage
+            auto issue_pv = [&](int j) -> bool {
+                if (!mbar_wait(&v_full[vs], vph, &s_abort, p.timeout_ns, flag)) return false;
+                if (!mbar_wait(&p_full[x], GP & 1, &s_abort, p.timeout_ns, flag)) return false;
                 tc_fence_after();
-                const uint32_t pa = smem_u32(sP + (size_t)x * PBYTES);
-                const uint32_t d = tmem_base + (uint32_t)x * 256u + 128u;
+                const uint32_t vb = smem_u32(sV + (size_t)vs * p.kv_bytes);
 #pragma unroll
                 for (int kb = 0; kb < BN / 16; ++kb)
-                    umma<false>(d, sw128_desc(pa + (kb >> 2) * BM * 128 + (kb & 3) * 32),
+                    umma<false>(o_tm, sw128_desc(pa + (kb >> 2) * BM * 128 + (kb & 3) * 32),
                                 sw128_desc_mn(vb + kb * 16 * 128, BN * 128), idesc_o, (j | kb) != 0);
                 umma_commit(&pv_done[x]);
-                ++GP[x];
+                umma_commit(&v_empty[vs]);
+                ++GP;
+                v_next();
+                return true;
+            };
+            // a K or V stage this tile does not use: wait for its fill, then release
+            auto skip_stage = [&](uint64_t* full, uint64_t* empty, int st, uint32_t ph) -> bool {
+                if (!mbar_wait(&full[st], ph, &s_abort, p.timeout_ns, flag)) return false;
+                mbar_arrive(&empty[st]);
                 return true;
             };
             for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
                 const Unit2 w = decode_unit2(u, p);
-                const int n[2] = {w.na, w.nb};
+                const int n = x == 0 ? w.na : w.nb;
                 const int nblk = w.nb > w.na ? w.nb : w.na;
                 if (!(ok = mbar_wait(q_full, qph, &s_abort, p.timeout_ns, flag))) break;
                 qph ^= 1;
-                // per key block j: S_A(j), S_B(j), then PV_A(j-1), PV_B(j-1)
-                for (int j = 0; ok && j <= nblk; ++j) {
-                    if (j < nblk) {
-                        if (!(ok = mbar_wait(&k_full[ks], kph, &s_abort, p.timeout_ns, flag))) break;
-                        const uint32_t kb = smem_u32(sK + (size_t)ks * p.kv_bytes);
-#pragma unroll
-                        for (int x = 0; x < 2; ++x)
-                            if (j < n[x] && !(ok = issue_s(x, kb))) break;
-                        if (!ok) break;
-                        umma_commit(&k_empty[ks]);
-                        if (++ks == p.nK) { ks = 0; kph ^= 1; }
-                        if (j + 1 == nblk) umma_commit(q_empty);   // the unit's last S was issued
+                if (n == 0) mbar_arrive(q_empty);
+                else if (!(ok = issue_s())) break;
+                if (n == 1) umma_commit(q_empty);
+                for (int j = 0; ok && j < n; ++j) {
+                    if (j + 1 < n) {
+                        if (!(ok = issue_s())) break;
+                        if (j + 2 == n) umma_commit(q_empty);   // this tile's last S was issued
                     }
-                    if (j > 0) {
-                        if (!(ok = mbar_wait(&v_full[vs], vph, &s_abort, p.timeout_ns, flag))) break;
-                        const uint32_t vb = smem_u32(sV + (size_t)vs * p.kv_bytes);
-#pragma unroll
-                        for (int x = 0; x < 2; ++x)
-                            if (j - 1 < n[x] && !(ok = issue_pv(x, vb, j - 1))) break;
-                        if (!ok) break;
-                        umma_commit(&v_empty[vs]);
-                        if (++vs == p.nV) { vs = 0; vph ^= 1; }
-                    }
+                    if (!(ok = issue_pv(j))) break;
+                }
+                // blocks of this unit that only the other tile uses (K loads run one ahead of V)
+                for (int j = n; ok && j < nblk; ++j) {
+                    if (!(ok = skip_stage(k_full, k_empty, ks, kph))) break;
+                    k_next();
+                    if (!(ok = skip_stage(v_full, v_empty, vs, vph))) break;
+                    v_next();
                 }
             }
         }
