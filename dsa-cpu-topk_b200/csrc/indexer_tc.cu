@@ -58,6 +58,7 @@ struct TcParams {
     int nA, nB;
     uint32_t a_bytes, b_bytes;
     int vec_store;
+    int vec8_store;             // rows 32-byte aligned: 256-bit score stores
     int elt;                    // bytes per q/k element: 2 (bf16) or 1 (e4m3)
     int stall;                  // test hook: the producer issues no loads, so every wait times out
     unsigned long long timeout_ns;
@@ -264,7 +265,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int64_t s0 = (int64_t)j * BN + half * 128;
             float* out = p.scores + ((int64_t)b * p.T_q + tq) * p.T_k + s0;
             const float NEG = -INFINITY;
-            if (p.vec_store && s0 + 128 <= p.T_k) {
+            if (p.vec8_store && s0 + 128 <= p.T_k) {
+                // 32-byte stores: each warp store writes whole sectors of its 32 rows
+#pragma unroll
+                for (int c = 0; c < 128; c += 8) {
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = (s0 + c + e <= t) ? acc[c + e] : NEG;
+                    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(out + c),
+                                 "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]),
+                                 "f"(v[7])
+                                 : "memory");
+                }
+            } else if (p.vec_store && s0 + 128 <= p.T_k) {
 #pragma unroll
                 for (int c = 0; c < 128; c += 4) {
                     float4 v;
@@ -361,6 +374,7 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     p.a_bytes = (uint32_t)(BM * DI * p.elt);
     p.b_bytes = (uint32_t)(BN * DI * p.elt);
     p.vec_store = (T_k % 4 == 0) ? 1 : 0;
+    p.vec8_store = (T_k % 8 == 0 && (reinterpret_cast<uintptr_t>(scores) & 31u) == 0) ? 1 : 0;
     // DSA_TEST_INDEXER_STALL=1: test hook for the timeout path (no loads are
     // issued, every wait runs out after 20 ms); never set in normal use
     p.stall = getenv("DSA_TEST_INDEXER_STALL") ? 1 : 0;
