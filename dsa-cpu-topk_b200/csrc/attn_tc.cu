@@ -68,6 +68,7 @@ struct AtParams {
     uint32_t q_bytes, kv_bytes;
     float sl2;            // scale * log2(e)
     int stall;            // test hook: the producer issues no loads, so every wait times out
+    int o_vec8;           // O 32-byte aligned: 256-bit output stores
     unsigned long long timeout_ns;
 };
 
@@ -770,7 +771,17 @@ __global__ void __launch_bounds__(NT2, 1)
                 uint32_t o[32];
                 tmem_ld32(o_col + c * 32, o);
                 tmem_wait_ld32(o);
-                if (row_ok) {
+                if (row_ok && p.o_vec8) {
+                    // 32-byte stores: whole sectors of each of the warp's 32 rows
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8)
+                        asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(orow + c * 32 + e),
+                                     "f"(__uint_as_float(o[e]) * inv), "f"(__uint_as_float(o[e + 1]) * inv),
+                                     "f"(__uint_as_float(o[e + 2]) * inv), "f"(__uint_as_float(o[e + 3]) * inv),
+                                     "f"(__uint_as_float(o[e + 4]) * inv), "f"(__uint_as_float(o[e + 5]) * inv),
+                                     "f"(__uint_as_float(o[e + 6]) * inv), "f"(__uint_as_float(o[e + 7]) * inv)
+                                     : "memory");
+                } else if (row_ok) {
 #pragma unroll
                     for (int e = 0; e < 32; e += 4)
                         *reinterpret_cast<float4*>(orow + c * 32 + e) =
@@ -882,6 +893,7 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
     // issued, every wait runs out after 20 ms); never set in normal use
     p.stall = getenv("DSA_TEST_ATTN_STALL") ? 1 : 0;
     p.timeout_ns = p.stall ? 20000000ull : 2000000000ull;
+    p.o_vec8 = (reinterpret_cast<uintptr_t>(O) & 31u) == 0 ? 1 : 0;
     if (units == 0) return DSA_OK;
 
     int dev = 0, optin = 0;
