@@ -48,6 +48,8 @@ constexpr int EPI_WARPS = 8;
 constexpr int NTHREADS = 64 + EPI_WARPS * 32;
 constexpr int MAX_TBLK = 1024;     // query blocks per batch (T_q <= 131072)
 constexpr uint32_t TMEM_COLS = 512;
+constexpr int CHUNK = 16;                          // score columns per TMA store (64 bytes)
+constexpr int STAGE_BYTES = 2 * 32 * CHUNK * 4;    // two 32-row chunk buffers per epilogue warp
 
 struct TcParams {
     float* scores;
@@ -59,6 +61,7 @@ struct TcParams {
     uint32_t a_bytes, b_bytes;
     int vec_store;
     int vec8_store;             // rows 32-byte aligned: 256-bit score stores
+    int tma_store;              // rows 16-byte aligned: staged TMA tensor stores of the scores
     int elt;                    // bytes per q/k element: 2 (bf16) or 1 (e4m3)
     int stall;                  // test hook: the producer issues no loads, so every wait times out
     unsigned long long timeout_ns;
@@ -83,7 +86,7 @@ __device__ __forceinline__ void decode_tile(int lin, const int* pref, const TcPa
 template <bool FP8>
 __global__ void __launch_bounds__(NTHREADS, 1)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                      const TcParams p) {
+                      const __grid_constant__ CUtensorMap tms, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int pref[MAX_TBLK + 1];
     __shared__ uint32_t tmem_slot;
@@ -92,7 +95,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                                ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = sA + (size_t)p.nA * p.a_bytes;
-    uint64_t* fullA = reinterpret_cast<uint64_t*>(sB + (size_t)p.nB * p.b_bytes);
+    uint8_t* sStage = sB + (size_t)p.nB * p.b_bytes;  // STAGE_BYTES per epilogue warp if tma_store
+    uint64_t* fullA = reinterpret_cast<uint64_t*>(sStage + (p.tma_store ? EPI_WARPS * STAGE_BYTES : 0));
     uint64_t* emptyA = fullA + p.nA;
     uint64_t* fullB = emptyA + p.nA;
     uint64_t* emptyB = fullB + p.nB;
@@ -215,6 +219,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         int tb = 0;
         uint32_t tph = 0;
+        uint32_t nstore = 0;   // TMA stores issued by this warp (buffer = nstore & 1)
+        uint8_t* stage = sStage + ew * STAGE_BYTES;
         bool ok = true;
         for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
             int b, i, j;
@@ -260,11 +266,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (++tb == 2) { tb = 0; tph ^= 1; }
                 }
             }
-            if (!ok || !row_ok) continue;
             const int64_t t = p.q_row0 + tq;
             const int64_t s0 = (int64_t)j * BN + half * 128;
-            float* out = p.scores + ((int64_t)b * p.T_q + tq) * p.T_k + s0;
             const float NEG = -INFINITY;
+            if (p.tma_store) {
+                // Each 32-row x 16-column chunk is written to a shared buffer
+                // (64-byte swizzle: 16-byte unit u of row r sits at unit
+                // u ^ ((r >> 1) & 3), so a quarter-warp's 16-byte writes hit
+                // distinct banks) and stored by one TMA tensor store; rows
+                // past T_q and columns past T_k are clipped by the tensor map.
+                if (!__all_sync(0xffffffffu, ok)) { ok = false; continue; }
+#pragma unroll
+                for (int ch = 0; ch < 128 / CHUNK; ++ch) {
+                    uint8_t* buf = stage + (nstore & 1) * (32 * CHUNK * 4);
+                    if (lane == 0) bulk_wait_read<1>();   // this buffer's previous store has read it
+                    __syncwarp();
+                    const int64_t c0 = s0 + ch * CHUNK;
+#pragma unroll
+                    for (int u = 0; u < CHUNK / 4; ++u) {
+                        float4 v;
+                        v.x = (c0 + u * 4 + 0 <= t) ? acc[ch * CHUNK + u * 4 + 0] : NEG;
+                        v.y = (c0 + u * 4 + 1 <= t) ? acc[ch * CHUNK + u * 4 + 1] : NEG;
+                        v.z = (c0 + u * 4 + 2 <= t) ? acc[ch * CHUNK + u * 4 + 2] : NEG;
+                        v.w = (c0 + u * 4 + 3 <= t) ? acc[ch * CHUNK + u * 4 + 3] : NEG;
+                        *reinterpret_cast<float4*>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = v;
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tms, buf, (int)c0, i * BM + quarter * 32, b);
+                        bulk_commit();
+                    }
+                    ++nstore;
+                }
+                continue;
+            }
+            if (!ok || !row_ok) continue;
+            float* out = p.scores + ((int64_t)b * p.T_q + tq) * p.T_k + s0;
             if (p.vec8_store && s0 + 128 <= p.T_k) {
                 // 32-byte stores: each warp store writes whole sectors of its 32 rows
 #pragma unroll
@@ -293,6 +331,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (s0 + c < p.T_k) out[c] = (s0 + c <= t) ? acc[c] : NEG;
             }
         }
+        if (p.tma_store && lane == 0) bulk_wait_all();   // staging buffers stay live until stored
     }
 
     tc_fence_before();
@@ -375,6 +414,11 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     p.b_bytes = (uint32_t)(BN * DI * p.elt);
     p.vec_store = (T_k % 4 == 0) ? 1 : 0;
     p.vec8_store = (T_k % 8 == 0 && (reinterpret_cast<uintptr_t>(scores) & 31u) == 0) ? 1 : 0;
+    // DSA_INDEXER_DIRECT_STORE=1: per-thread global stores instead of TMA stores
+    p.tma_store = (T_k % 4 == 0 && (reinterpret_cast<uintptr_t>(scores) & 15u) == 0 &&
+                   !getenv("DSA_INDEXER_DIRECT_STORE"))
+                      ? 1
+                      : 0;
     // DSA_TEST_INDEXER_STALL=1: test hook for the timeout path (no loads are
     // issued, every wait runs out after 20 ms); never set in normal use
     p.stall = getenv("DSA_TEST_INDEXER_STALL") ? 1 : 0;
@@ -392,11 +436,18 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     const size_t fixed = 1024 + 256;
     const char* env_nb = getenv("DSA_TC_NB");  // ring depth of the key operand (1 or 2)
     p.nB = (env_nb && env_nb[0] == '1') ? 1 : 2;
-    if (kMaxSmem < fixed + (size_t)p.nB * p.b_bytes + 2 * (size_t)p.a_bytes) p.nB = 1;
-    p.nA = (int)((kMaxSmem - fixed - (size_t)p.nB * p.b_bytes) / p.a_bytes);
+    // the staging buffers take 32 KB; the A ring gives up a stage for them
+    // (two A stages keep the tensor pipe as busy as three)
+    size_t stage = p.tma_store ? (size_t)EPI_WARPS * STAGE_BYTES : 0;
+    if (stage && kMaxSmem < fixed + stage + (size_t)p.nB * p.b_bytes + 2 * (size_t)p.a_bytes) {
+        p.tma_store = 0;
+        stage = 0;
+    }
+    if (kMaxSmem < fixed + stage + (size_t)p.nB * p.b_bytes + 2 * (size_t)p.a_bytes) p.nB = 1;
+    p.nA = (int)((kMaxSmem - fixed - stage - (size_t)p.nB * p.b_bytes) / p.a_bytes);
     if (p.nA > 8) p.nA = 8;
     if (p.nA < 2) return -100;
-    const size_t smem = fixed + (size_t)p.nA * p.a_bytes + (size_t)p.nB * p.b_bytes;
+    const size_t smem = fixed + stage + (size_t)p.nA * p.a_bytes + (size_t)p.nB * p.b_bytes;
 
     if (fill_upper) {
         fill_upper_kernel<<<(unsigned)(B * T_q), 256, 0, stream>>>(scores, T_q, T_k, q_row0);
@@ -405,7 +456,7 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     }
     if (p.total_tiles == 0) return DSA_OK;
 
-    CUtensorMap tmq, tmk;
+    CUtensorMap tmq, tmk, tms;
     {
         const cuuint64_t dims[4] = {(cuuint64_t)DI, (cuuint64_t)HI, (cuuint64_t)T_q, (cuuint64_t)B};
         const cuuint64_t e = (cuuint64_t)p.elt;
@@ -422,11 +473,22 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
         int rc = encode_map(&tmk, k, 3, dims, str, box, "k", p.elt);
         if (rc) return rc;
     }
+    if (p.tma_store) {
+        // scores [B, T_q, T_k] fp32, box 16 columns x 32 rows, 64-byte swizzle
+        const cuuint64_t dims[3] = {(cuuint64_t)T_k, (cuuint64_t)T_q, (cuuint64_t)B};
+        const cuuint64_t str[2] = {(cuuint64_t)T_k * 4, (cuuint64_t)T_q * T_k * 4};
+        const cuuint32_t box[3] = {(cuuint32_t)CHUNK, 32, 1};
+        int rc = tc::encode_map(&tms, scores, 3, dims, str, box, "indexer_tc: scores",
+                                CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
+    } else {
+        tms = tmk;  // unused
+    }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return fail(DSA_ERR_CUDA, "indexer_tc: cannot set dynamic shared memory size");
     int grid = num_sms();
     if (grid > p.total_tiles) grid = p.total_tiles;
-    kern<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, p);
+    kern<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, tms, p);
     return check_launch("indexer_tc_kernel");
 }
 

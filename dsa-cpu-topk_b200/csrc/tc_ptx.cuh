@@ -81,6 +81,25 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
         : "memory");
 }
+// TMA tile store shared -> global (3-D map), tracked in the thread's bulk group.
+// Elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until all of this thread's bulk groups have completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,
 // 8-row core groups 1024 bytes apart (SBO), sm_100 descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -275,15 +294,15 @@ inline EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Tiled map with 128-byte swizzle, zero fill out of bounds (no multicast use).
+// Tiled map (128-byte swizzle unless given), zero fill out of bounds (no multicast use).
 inline int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
                       const cuuint64_t* strides, const cuuint32_t* box, const std::string& what,
-                      CUtensorMapDataType dt) {
+                      CUtensorMapDataType dt, CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(DSA_ERR_CUDA, what + ": cuTensorMapEncodeTiled not available");
     const CUresult r = enc(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(DSA_ERR_CUDA, what + ": cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
