@@ -76,9 +76,10 @@ __device__ __forceinline__ void unpack16<__half>(const uint4& v, float* out) {
 // Order-preserving map float -> uint32 (larger float -> larger key).
 // -0.0 is folded onto +0.0 so that key equality matches float ==.
 __device__ __forceinline__ uint32_t f2key(float x) {
-    uint32_t b = __float_as_uint(x);
-    if ((b << 1) == 0) b = 0;  // +-0 -> +0
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    // negative: ~b, positive: b | sign; then -0 (key 0x7fffffff) -> +0's key
+    const uint32_t b = __float_as_uint(x);
+    const uint32_t k = b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+    return k == 0x7fffffffu ? 0x80000000u : k;
 }
 __device__ __forceinline__ float key2f(uint32_t k) {
     uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;

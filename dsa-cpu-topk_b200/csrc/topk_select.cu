@@ -344,7 +344,7 @@ __device__ __forceinline__ void emit_bits(const TopkArgs& a, int64_t row, const 
 }
 
 template <int BLOCK, bool CACHED>
-__global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
+__global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_kernel(TopkArgs a) {
     constexpr int NW = BLOCK / 32;
     constexpr int S0 = 21;  // shift of the first digit
     extern __shared__ uint4 dyn4[];
@@ -435,6 +435,10 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
         const uint32_t d0 = res[0];
         uint32_t krem = res[1];
         const bool use_cand = hist[(NB_TOP - 1) - d0] <= (uint32_t)a.cand_max;
+        // no key in bins 0-3 or 2044-2047 (NaNs, infinities and their
+        // neighbours): float order is key order on this row
+        const bool plain = (hist[0] | hist[1] | hist[2] | hist[3] | hist[NB_TOP - 4] | hist[NB_TOP - 3] |
+                            hist[NB_TOP - 2] | hist[NB_TOP - 1]) == 0u;
         __syncthreads();
 
         // warp w owns groups [w*gseg, min((w+1)*gseg, g4))
@@ -462,6 +466,48 @@ __global__ void __launch_bounds__(BLOCK) topk_cached_kernel(TopkArgs a) {
             // loop and break tests use the warp's first group (g0 - lane), so
             // whole warps run the shuffles; gw is a multiple of 8, so the 8
             // lanes of a word are all inside or all past it
+            if (!CACHED && plain && d0 >= 4 && d0 <= NB_TOP - 5) {
+                // float compares against the bin edges (finite floats here);
+                // positions past `valid` read as -inf, below bin d0
+                const float hi_f = key2f(hi_key), lo_f = key2f(lo);
+                const float4* src4 = reinterpret_cast<const float4*>(src);
+                for (int g0 = tid; g0 - lane < gw; g0 += PIPE * BLOCK) {
+                    float4 xb[PIPE];
+#pragma unroll
+                    for (int u = 0; u < PIPE; ++u) {
+                        const int g = g0 + u * BLOCK;
+                        if (a.vec_ok && 4 * g + 3 < valid) {
+                            xb[u] = __ldg(src4 + g);
+                        } else {
+                            float e[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) e[j] = 4 * g + j < valid ? __ldg(src + 4 * g + j) : __uint_as_float(0xff800000u);
+                            xb[u] = make_float4(e[0], e[1], e[2], e[3]);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < PIPE; ++u) {
+                        const int g = g0 + u * BLOCK;
+                        if (g - lane >= gw) break;
+                        const float e[4] = {xb[u].x, xb[u].y, xb[u].z, xb[u].w};
+                        uint32_t nib = 0;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) nib |= (uint32_t)(e[j] >= hi_f) << j;
+                        uint32_t wd = nib << (4 * (lane & 7));
+                        wd |= __shfl_xor_sync(0xffffffffu, wd, 1);
+                        wd |= __shfl_xor_sync(0xffffffffu, wd, 2);
+                        wd |= __shfl_xor_sync(0xffffffffu, wd, 4);
+                        if ((lane & 7) == 0 && g < gw) out[g >> 3] = wd;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (e[j] >= lo_f && e[j] < hi_f) {
+                                const uint32_t at = atomicAdd(&n_cand, 1u);
+                                cand_key[at] = f2key(e[j]);
+                                cand_pos[at] = 4 * g + j;
+                            }
+                    }
+                }
+            } else
             for (int g0 = tid; g0 - lane < gw; g0 += PIPE * BLOCK) {
                 uint4 kb[PIPE];
 #pragma unroll

@@ -193,6 +193,31 @@ def test_topk_bitmap_special_values(cuda, k):
     assert torch.equal(pop, cnt.long())
 
 
+@pytest.mark.parametrize("k", [1, 700, 2048, 9999])
+def test_topk_bitmap_bin_edges_long_rows(cuda, k):
+    """20,000-entry rows (the kernel variant c5 uses) whose values sit on the
+    edges of the first-digit bins (1.0, 1.25, -0.75, ... have two mantissa
+    bits), with both zeros and denormals: the float-compare sweep must keep
+    exactly the keys a key compare keeps, with the threshold of torch.topk."""
+    from topk import topk_select, topk_select_bitmap
+    g = torch.Generator(device=cuda).manual_seed(k)
+    edges = torch.tensor([0.5, 0.75, 1.0, 1.25, 1.5, 1.75, 2.0, -0.5, -0.75, -1.0, 0.0, -0.0,
+                          1e-40, -1e-40, 3.0, 2.5], device=cuda)
+    n = 20000
+    pick = torch.randint(0, len(edges), (2, 8, n), generator=g, device=cuda)
+    sc = edges[pick]
+    noisy = torch.rand(2, 8, n, generator=g, device=cuda) < 0.3
+    sc = torch.where(noisy, torch.randn(2, 8, n, generator=g, device=cuda), sc)
+    sc[1, 3] = torch.randn(n, generator=g, device=cuda) * 1e-39      # denormal row
+    thr, cnt, bits = topk_select_bitmap(sc, k, causal=False)
+    thr2, _, cnt2 = topk_select(sc, k, causal=False, idx_cap=32)
+    assert torch.equal(thr, thr2) and torch.equal(cnt, cnt2)
+    kth = sc.topk(k, dim=-1).values[..., -1:]
+    assert torch.equal(thr.view_as(kth), kth)
+    ref = torch.from_numpy(_bits_ref(sc.cpu(), thr.cpu(), n, bits.shape[1])).to(cuda)
+    assert torch.equal(bits, ref)
+
+
 @pytest.mark.parametrize("levels", [3, 40])
 def test_topk_bitmap_threshold_bin_overflow(cuda, levels):
     """Rows of 4K-8K entries whose threshold bin holds more keys than the
