@@ -716,15 +716,13 @@ __global__ void __launch_bounds__(NT2, 1)
                 }
                 // P_X's buffer and O_X: PV_X(j-1) must have landed
                 if (j > 0 && !(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
-                // P = 2^(x*sl2 - m): the exponent in fp32 (packed FMA), rounded to the
-                // 16-bit input type, two exponentials per MUFU op; l sums the
-                // rounded P values that the PV product consumes.  16-byte slot i
-                // of the 128-byte swizzled row holds keys 64*cc + 8*i .. +7.
+                // P = 2^(x*sl2 - m): the exponent in fp32 (packed FMA), 2^ in fp32
+                // on the MUFU, rounded to the 16-bit input type for the PV product;
+                // l sums the fp32 values (packed adds).  16-byte slot i of the
+                // 128-byte swizzled row holds keys 64*cc + 8*i .. +7.
                 const float mu = m_run == kNegInf ? 0.f : m_run;
                 const float2 sl2v = make_float2(p.sl2, p.sl2), nmu = make_float2(-mu, -mu);
-                float lp[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) lp[e] = 0.f;
+                uint64_t lp[4] = {0ull, 0ull, 0ull, 0ull};   // packed fp32 pairs
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
@@ -735,14 +733,21 @@ __global__ void __launch_bounds__(NT2, 1)
                             const int c = cc * 64 + i * 8 + 2 * e;
                             const float2 xx =
                                 fma2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2v, nmu);
-                            pk[e] = ex2_pair<F16>(xx.x, xx.y);
-                            add_pair<F16>(lp[2 * e], lp[2 * e + 1], pk[e]);
+                            pk[e] = ex2_pair_sum<F16>(xx.x, xx.y, lp[e]);
                         }
                         *reinterpret_cast<uint4*>(prow_base + cc * BM * 128 + ((i ^ (row & 7)) << 4)) =
                             make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     }
                 }
-                l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+                {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        f[2 * e] = __uint_as_float((uint32_t)lp[e]);
+                        f[2 * e + 1] = __uint_as_float((uint32_t)(lp[e] >> 32));
+                    }
+                    l += ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
+                }
                 // rescale O_X (after the row's S values are dead); PV_X(j) is
                 // issued only after p_full, so it sees the rescaled O
                 if (j > 0 && __any_sync(0xffffffffu, need)) {

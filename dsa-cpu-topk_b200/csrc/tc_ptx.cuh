@@ -243,34 +243,20 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
           "l"(*reinterpret_cast<uint64_t*>(&c)));
     return *reinterpret_cast<float2*>(&d);
 }
-// 2^x of two values rounded to a 16-bit pair (lo = x0, hi = x1): bf16x2
-// (flushes denormal results) or f16x2, on the MUFU, two results per op
+// 2^x0, 2^x1 in fp32 on the MUFU (denormal results flushed), rounded to a
+// 16-bit pair (lo = x0): bf16x2 or f16x2; the fp32 values are added into the
+// packed accumulator acc (lo += 2^x0, hi += 2^x1) with one add.rn.f32x2
 template <bool F16>
-__device__ __forceinline__ uint32_t ex2_pair(float x0, float x1) {
-    uint32_t h, y;
-    if constexpr (F16) {
-        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
-        asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(h));
-    } else {
-        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
-        asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(h));
-    }
+__device__ __forceinline__ uint32_t ex2_pair_sum(float x0, float x1, uint64_t& acc) {
+    float p0, p1;
+    uint32_t y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p0) : "f"(x0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p1) : "f"(x1));
+    if constexpr (F16) asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(y) : "f"(p1), "f"(p0));
+    else asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(y) : "f"(p1), "f"(p0));
+    const uint64_t v = (uint64_t)__float_as_uint(p0) | ((uint64_t)__float_as_uint(p1) << 32);
+    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc) : "l"(v));
     return y;
-}
-// a0 += lo(v), a1 += hi(v): the two 16-bit values of v widened to fp32
-template <bool F16>
-__device__ __forceinline__ void add_pair(float& a0, float& a1, uint32_t v) {
-    if constexpr (F16) {
-        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-            "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
-            : "+f"(a0), "+f"(a1)
-            : "r"(v));
-    } else {
-        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-            "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
-            : "+f"(a0), "+f"(a1)
-            : "r"(v));
-    }
 }
 
 // ---- host: tensor maps -------------------------------------------------------

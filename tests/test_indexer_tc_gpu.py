@@ -35,6 +35,10 @@ def simt_scores(q, k, w, **kw):
     (1, 129, 1001, 872, 8, 128),    # row block at an offset, T_k % 4 != 0
     (3, 1, 513, 512, 2, 64),        # single query row
     (1, 2048, 2048, 0, 64, 128),    # c5 head shapes
+    # TMA score stores (T_k % 4 == 0) at row offsets with several batches:
+    # ragged T_q (rows past it clipped at the batch edge) and a partial last chunk
+    (2, 200, 1004, 804, 4, 64),
+    (2, 72, 1028, 956, 8, 128),
 ])
 def test_tc_matches_simt_and_oracle(cuda, B, T_q, T_k, q0, HI, DI):
     g = torch.Generator().manual_seed(T_q + 7 * HI)
