@@ -49,6 +49,11 @@ CONFIGS = {
     # c5 with the indexer inputs in FP8 (e4m3) as in the DeepSeek-V3.2 paper; not a BASELINE config
     "c5_fp8": dict(B=1, T=32768, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16", idx_dtype="fp8",
                    desc="c5 with e4m3 indexer q/k (FP8 indexer), bf16 Q/K/V"),
+    # c5 with structured selections: indexer q/k carry a positional code, so each
+    # query keeps a local window of keys plus strided "sink" blocks (most key
+    # blocks of a query tile hold no kept key); not a BASELINE config
+    "c5_local": dict(B=1, T=32768, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16", structured=True,
+                     desc="c5 shapes, structured selections (local window + strided sink blocks), bf16"),
     # c5's head shapes at T=8192 (~2 GB on the device): the small case the ncu captures use
     "c5_t8k": dict(B=1, T=8192, HI=64, DI=128, HQ=16, D=128, k=2048, dtype="bf16",
                    desc="c5 head shapes at T8192 (profiling case), bf16, causal"),
@@ -145,63 +150,108 @@ def make_inputs_device(cfg, B, dev, seed):
         return (torch.randn(shape, generator=g, device=dev) * scale).to(dtype)
 
     it = DT[cfg.get("idx_dtype", cfg["dtype"])]
+    if cfg.get("structured"):
+        # positional code: <q_t, k_s> = mean_i cos(2 pi (t - s) / lambda_i) peaks at s = t
+        # and decays with distance; one more dimension lifts keys s % 4096 < 128
+        nf = (DI - 2) // 2
+        pos = torch.arange(T, device=dev, dtype=torch.float32)
+        lam = 2.0 ** torch.linspace(6.0, math.log2(T), nf, device=dev)
+        ang = 2 * math.pi * pos[:, None] / lam[None, :]
+        enc = torch.cat([ang.cos(), ang.sin()], dim=1) / math.sqrt(nf)            # [T, 2 nf]
+        sink = ((pos % 4096) < 128).float()[:, None] * 0.8
+        kk = torch.cat([enc, sink, torch.zeros(T, 1, device=dev)], dim=1)
+        qq = torch.cat([enc, torch.ones(T, 1, device=dev), torch.zeros(T, 1, device=dev)], dim=1)
+        k_idx = (kk[None] + 0.02 * torch.randn((B, T, DI), generator=g, device=dev)).to(it)
+        q_idx = (qq[None, :, None, :] + 0.02 * torch.randn((B, T, HI, DI), generator=g, device=dev)).to(it)
+        w_idx = torch.rand((B, T, HI), generator=g, device=dev) / HI
+        return (q_idx, k_idx, w_idx, rnd((B, T, HQ, D)), rnd((B, T, HQ, D)), rnd((B, T, HQ, D)))
     return (rnd((B, T, HI, DI), dtype=it), rnd((B, T, DI), dtype=it), rnd((B, T, HI), 1 / math.sqrt(HI), torch.float32),
             rnd((B, T, HQ, D)), rnd((B, T, HQ, D)), rnd((B, T, HQ, D)))
 
 
 class Pipeline:
-    """Preallocated buffers and the three C-ABI stage calls for some row blocks."""
+    """Preallocated buffers and the three C-ABI stage calls for some row blocks.
+
+    Two equal row blocks of one sequence (a rank's zig-zag pair under strong
+    scaling) run as ONE launch per stage: the blocks are stacked as a batch of
+    2 with the key side shared (batch stride 0) and row_bstep = the distance
+    between their first rows.  Anything else runs one launch per block."""
 
     def __init__(self, inputs, blocks, k):
         import _native
         from topk import idx_cap_for
         self.n = _native
         q, kk, w, Q, K, V = inputs
-        self.k_idx, self.K, self.V = kk, K, V
         B, T = Q.shape[:2]
         self.k = min(k, T)
         self.cap = idx_cap_for(self.k, T)
         self.parts = []
         dev = Q.device
-        for blk in blocks:
-            Tq = blk.stop - blk.start
-            sl = slice(blk.start, blk.stop)
-            p = dict(q0=blk.start, Tq=Tq, q=q[:, sl].contiguous(), w=w[:, sl].contiguous(),
-                     Q=Q[:, sl].contiguous(),
-                     scores=torch.empty((B, Tq, T), device=dev, dtype=torch.float32),
-                     thr=torch.empty(B * Tq, device=dev, dtype=torch.float32),
-                     cnt=torch.empty(B * Tq, device=dev, dtype=torch.int32),
-                     idx=torch.empty((B * Tq, self.cap), device=dev, dtype=torch.int32),
-                     O=torch.empty((B, Tq, Q.shape[2], V.shape[3]), device=dev, dtype=torch.float32))
+        lens = {b.stop - b.start for b in blocks}
+        self.stacked = len(blocks) == 2 and B == 1 and len(lens) == 1
+        if self.stacked:
+            a, b = blocks
+            st = lambda x: torch.cat([x[:, a.start:a.stop], x[:, b.start:b.stop]]).contiguous()
+            groups = [dict(q0=a.start, bstep=b.start - a.start, Tq=a.stop - a.start, NB=2,
+                           q=st(q), w=st(w), Q=st(Q))]
+            exp = lambda x: x.expand(2, *x.shape[1:])
+            self.k_idx, self.K, self.V = exp(kk), exp(K), exp(V)
+        else:
+            groups = [dict(q0=blk.start, bstep=0, Tq=blk.stop - blk.start, NB=B,
+                           q=q[:, blk.start:blk.stop].contiguous(), w=w[:, blk.start:blk.stop].contiguous(),
+                           Q=Q[:, blk.start:blk.stop].contiguous()) for blk in blocks]
+            self.k_idx, self.K, self.V = kk, K, V
+        for p in groups:
+            NB, Tq = p["NB"], p["Tq"]
+            p.update(scores=torch.empty((NB, Tq, T), device=dev, dtype=torch.float32),
+                     thr=torch.empty(NB * Tq, device=dev, dtype=torch.float32),
+                     cnt=torch.empty(NB * Tq, device=dev, dtype=torch.int32),
+                     idx=torch.empty((NB * Tq, self.cap), device=dev, dtype=torch.int32),
+                     O=torch.empty((NB, Tq, Q.shape[2], V.shape[3]), device=dev, dtype=torch.float32))
             self.parts.append(p)
         # stage 3 on the tensor cores (kept-set bitmap + masked flash attention)
         # where the dtype and head size allow, else the gather over kept lists
         self.tc = _native.attn_tc_supported(Q, V) and os.environ.get("DSA_ATTN_GATHER") != "1"
         self.words = _native.bitmap_words(T)
+        self.v16 = False
         if self.tc:
             for p in self.parts:
-                p["bits"] = torch.empty((B * p["Tq"], self.words), device=dev, dtype=torch.int32)
+                p["bits"] = torch.empty((p["NB"] * p["Tq"], self.words), device=dev, dtype=torch.int32)
+                # stage 3's workspace: block summary, fp16 copy of V (bf16)
+                nws = _native.sparse_attn_bitmap_workspace_bytes(p["NB"], p["Tq"], T, Q.shape[2], V.shape[3],
+                                                                 _native.dtype_code(Q))
+                p["ws"] = torch.empty(nws, device=dev, dtype=torch.uint8) if nws else None
+                self.v16 = self.v16 or bool(nws)
         self.stage_names = ["indexer", "topk", "sparse_attn"]
-        self.launches_per_step = len(self.stage_names) * len(self.parts)
+        # stage 3 with its workspace: block summary (+ |V| max and fp16 conversion
+        # for bf16) + attention
+        v16 = self.tc and Q.dtype == torch.bfloat16
+        self.launches_per_step = (len(self.stage_names) + (1 if self.v16 else 0) + (2 if v16 else 0)) * \
+            len(self.parts)
         # opt-in one-launch kernel for short sequences (DSA_FUSED_SMALL=1)
-        self.fused = T <= 512 and bool(os.environ.get("DSA_FUSED_SMALL"))
+        self.fused = T <= 512 and bool(os.environ.get("DSA_FUSED_SMALL")) and not self.stacked
         if self.fused:
             from dsa_attention import forward_workspace_bytes
-            self.q_all, self.w_all = q, w
-            self.Q_all = Q
             self.ws = [torch.empty(forward_workspace_bytes(B, p["Tq"], T, self.k), device=dev, dtype=torch.uint8)
                        for p in self.parts]
             self.launches_per_step = len(self.parts)
             self.stage_names = ["fused_forward"]
         self.step(None)  # untimed: fills the kept counts used for accounting
         for p in self.parts:
-            B, Tq, T = p["scores"].shape
+            NB, Tq, T = p["scores"].shape
             if self.tc or self.fused:
-                self.n.topk_select(p["scores"], B * Tq, T, T, self.k, p["thr"], None, p["cnt"], 0,
-                                   causal=True, rows_per_batch=Tq, q_row0=p["q0"])
+                self.n.topk_select_ex(p["scores"], NB * Tq, T, T, self.k, p["thr"], None, p["cnt"], 0,
+                                      causal=True, rows_per_batch=Tq, q_row0=p["q0"], row_bstep=p["bstep"])
+
+    def out_rows(self):
+        """This rank's output rows in block order, [B, rows, HQ, D]."""
+        if self.stacked:
+            O = self.parts[0]["O"]
+            return torch.cat([O[0:1], O[1:2]], dim=1)
+        return torch.cat([p["O"] for p in self.parts], dim=1)
 
     def step(self, ev=None):
-        """One forward over every row block; ev[i][j] brackets stage j of block i."""
+        """One forward over every row block; ev[i][j] brackets stage j of part i."""
         n = self.n
         for i, p in enumerate(self.parts):
             rec = (lambda j: ev[i][j].record()) if ev is not None else (lambda j: None)
@@ -211,20 +261,24 @@ class Pipeline:
                           q_row0=p["q0"])
                 rec(1)
                 continue
-            n.indexer_scores(p["q"], self.k_idx, p["w"], p["scores"], q_row0=p["q0"], fill_upper=False)
+            q0, bs = p["q0"], p["bstep"]
+            n.indexer_scores_ex(p["q"], self.k_idx, p["w"], p["scores"], q_row0=q0, row_bstep=bs,
+                                fill_upper=False)
             rec(1)
-            B, Tq, T = p["scores"].shape
+            NB, Tq, T = p["scores"].shape
             if self.tc:
-                n.topk_select_bitmap(p["scores"], self.k, p["thr"], p["bits"], causal=True, q_row0=p["q0"])
+                n.topk_select_ex(p["scores"], NB * Tq, T, T, self.k, p["thr"], None, None, 0, p["bits"],
+                                 causal=True, rows_per_batch=Tq, q_row0=q0, row_bstep=bs)
                 rec(2)
-                n.sparse_attn_bitmap(p["bits"], p["Q"], self.K, self.V, p["O"], q_row0=p["q0"])
+                n.sparse_attn_bitmap_ex(p["bits"], p["Q"], self.K, self.V, p["O"], q_row0=q0, row_bstep=bs,
+                                        workspace=p["ws"])
                 rec(3)
                 continue
-            n.topk_select(p["scores"], B * Tq, T, T, self.k, p["thr"], p["idx"], p["cnt"], self.cap,
-                          causal=True, rows_per_batch=Tq, q_row0=p["q0"])
+            n.topk_select_ex(p["scores"], NB * Tq, T, T, self.k, p["thr"], p["idx"], p["cnt"], self.cap,
+                             causal=True, rows_per_batch=Tq, q_row0=q0, row_bstep=bs)
             rec(2)
-            n.sparse_attn(p["idx"], p["cnt"], self.cap, p["scores"], p["thr"], p["Q"], self.K, self.V,
-                          p["O"], q_row0=p["q0"])
+            n.sparse_attn_ex(p["idx"], p["cnt"], self.cap, p["scores"], p["thr"], p["Q"], self.K, self.V,
+                             p["O"], q_row0=q0, row_bstep=bs)
             rec(3)
 
     def algorithmic(self, cfg):
@@ -233,22 +287,24 @@ class Pipeline:
         HI, DI, HQ, D = cfg["HI"], cfg["DI"], cfg["HQ"], cfg["D"]
         flops = topk_b = attn_b = attn_f = tile_f = 0
         for p in self.parts:
-            B, Tq, T = p["scores"].shape
-            t = torch.arange(p["q0"], p["q0"] + Tq, dtype=torch.float64)
-            valid = torch.clamp(t + 1, max=T).sum().item() * B
+            NB, Tq, T = p["scores"].shape
+            rows = NB * Tq
             sel = p["cnt"].double().sum().item()
-            rows = B * Tq
-            flops += 2.0 * HI * DI * valid
-            topk_b += 4.0 * valid + (4.0 * rows + 4.0 * rows * self.words if self.tc
-                                     else 8.0 * rows + 4.0 * sel)
+            for bb in range(NB):
+                r0 = p["q0"] + bb * p["bstep"]          # this batch's first query row
+                t = torch.arange(r0, r0 + Tq, dtype=torch.float64)
+                valid = torch.clamp(t + 1, max=T).sum().item()
+                flops += 2.0 * HI * DI * valid
+                topk_b += 4.0 * valid
+                # tensor-core stage 3: every 128x128 (query, key) tile up to the
+                # diagonal is two MMAs of 2*128*128*D FLOPs per head
+                for qt in range((Tq + 127) // 128):
+                    t_end = r0 + min((qt + 1) * 128, Tq)
+                    nblk = min((t_end - 1) // 128 + 1, (T + 127) // 128)
+                    tile_f += HQ * nblk * 4.0 * 128 * 128 * D
+            topk_b += (4.0 * rows + 4.0 * rows * self.words if self.tc else 8.0 * rows + 4.0 * sel)
             attn_b += sel * HQ * 2 * D * elt + rows * HQ * D * (elt + 4) + 4.0 * sel + 4.0 * rows
             attn_f += sel * HQ * 4.0 * D
-            # tensor-core stage 3: every 128x128 (query, key) tile up to the
-            # diagonal is two MMAs of 2*128*128*D FLOPs per head
-            for qt in range((Tq + 127) // 128):
-                t_end = p["q0"] + min((qt + 1) * 128, Tq)
-                nblk = min((t_end - 1) // 128 + 1, (T + 127) // 128)
-                tile_f += B * HQ * nblk * 4.0 * 128 * 128 * D
         return dict(indexer_flops=flops, topk_bytes=topk_b, attn_bytes=attn_b, attn_flops=attn_f,
                     attn_tile_flops=tile_f)
 
@@ -304,7 +360,19 @@ def cpu_reference_rate(ctx, cfg, seconds: float, chunk: int):
 
 
 def cpu_kind(ctx):
-    return "reference" if ctx["ext"] is not None else "port"
+    """"port": the indexer and attention legs are this repo's restatement of the
+    reference's torch variant; only the top-K leg is the reference's own code."""
+    return "port"
+
+
+def cpu_extra(ctx, cfg, rows):
+    """What the CPU number is made of, and that it is a rate over sampled rows."""
+    return {"components": {
+                "indexer": "port: oracle/dsa_oracle.py restatement of lightning_indexer.py:26-33 (torch, fp32)",
+                "topk": ("reference: topk_avx512.cpp compiled from its sources (oracle/_ref)"
+                         if ctx["ext"] is not None else "port: torch.topk (AVX-512 extension unavailable)"),
+                "attention": "port: oracle/dsa_oracle.py restatement of dsa_attention.py:46-51 (torch, fp32)"},
+            "extrapolated": True, "rows_sampled": int(rows), "rows_per_step": cfg["B"] * cfg["T"]}
 
 
 def cpu_sample_text(ctx, cfg, rows, el):
@@ -315,7 +383,8 @@ def cpu_sample_text(ctx, cfg, rows, el):
             f"OMP/torch threads={ctx['threads']}")
 
 
-CHUNK = {"c1": 512, "c3_b64_k128": 512, "c4": 64, "c5": 16, "c5_t8k": 32, "c5_t16k": 32}
+CHUNK = {"c1": 512, "c3_b64_k128": 512, "c4": 64, "c5": 16, "c5_local": 16, "c5_fp8": 16, "c5_t8k": 32,
+         "c5_t16k": 32}
 
 
 # --------------------------------------------------------------------------
@@ -345,6 +414,15 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -364,6 +442,10 @@ def base_line(args, cfg, world, value, ms, unit="query-tokens/s"):
                    "HQ": cfg["HQ"], "D": cfg["D"],
                    "parallelism": (f"batch-shard x{world}" if args.scaling == "weak"
                                    else f"query-row zig-zag x{world}"),
+                   "row_blocks": ("each rank: its own whole sequences" if args.scaling == "weak" else
+                                  "one sequence; rank r owns row blocks r and 2N-1-r of 2N, run as one "
+                                  "launch per stage (B=2 row blocks, shared key side)" if world > 1 else
+                                  "one sequence, all rows on one GPU"),
                    "l2": "inputs larger than L2" if cfg["T"] >= 8192 else
                          "L2 flushed between steps (256 MB write)"},
     }
@@ -376,7 +458,7 @@ def run_b200(args, cfg, world, rank, local):
     B, T = cfg["B"], cfg["T"]
     seed = 1000 * (rank if args.scaling == "weak" else 0)
     inputs = make_inputs_device(cfg, B, dev, seed)
-    if args.scaling == "weak":
+    if args.scaling == "weak" or world == 1:
         blocks = [sharding.RowBlock(0, T)]
     else:
         blocks = sharding.zigzag_plan(T, world)[rank]
@@ -450,12 +532,20 @@ def run_b200(args, cfg, world, rank, local):
     # rooflines of each stage (algorithmic work / measured average duration)
     hbm, tflops, src = load_peaks()
     peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if src == "measured" else {}
-    tf_sust = peaks.get("bf16_tflops_sustained", 1390.7 if src == "fallback" else tflops)
+    tf_sust = peaks.get("bf16_tflops_sustained", 1400.0 if src == "fallback" else tflops)
+    # The bf16 denominator follows the clocks this run saw: the burst GEMM peak
+    # when the SM clock stayed within 5% of its maximum (a burst), else the
+    # sustained (power-capped) one.  Both fractions are reported.
+    at_max = bool(clk.get("sm_mhz") and clk.get("sm_max_mhz") and clk["sm_mhz"] >= 0.95 * clk["sm_max_mhz"])
+    tf_peak = tflops if at_max else tf_sust
+    tf_label = (f"burst bf16 GEMM peak ({'measured' if src == 'measured' else 'fallback'}; SM clock median "
+                f"{clk.get('sm_mhz')} of {clk.get('sm_max_mhz')} MHz)" if at_max else
+                "sustained bf16 GEMM peak (SM clock below 95% of max)")
     alg = pipe.algorithmic(cfg)
     traffic = load_traffic().get(args.config, {})
     stages = {
         "indexer": dict(bound="tensor", achieved=alg["indexer_flops"] / (stage_ms[0] / 1e3) / 1e12,
-                        peak=tf_sust * (2 if cfg.get("idx_dtype") == "fp8" else 1), unit="TFLOP/s",
+                        peak=tf_peak * (2 if cfg.get("idx_dtype") == "fp8" else 1), unit="TFLOP/s",
                         ms=stage_ms[0],
                         kernel=("indexer_tc (e4m3, kind::f8f6f4)" if cfg.get("idx_dtype") == "fp8" else
                                 "indexer_tc" if cfg["dtype"] == "bf16" else "indexer_simt (fp32 CUDA cores)"),
@@ -469,14 +559,23 @@ def run_b200(args, cfg, world, rank, local):
     if pipe.tc:
         stages["topk"]["kernel"] = "topk_cached_kernel (threshold + kept-set bitmap)"
         stages["sparse_attn"] = dict(
-            bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_sust,
+            bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_peak,
             unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc2_kernel", traffic=traffic.get("sparse_attn"),
-            note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs")
+            note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs",
+            useful_tflops=alg["attn_flops"] / (stage_ms[2] / 1e3) / 1e12,
+            useful_fraction_of_tile_flops=alg["attn_flops"] / max(alg["attn_tile_flops"], 1.0))
+        stages["sparse_attn"]["useful_frac"] = stages["sparse_attn"]["useful_tflops"] / tf_peak
     for v in stages.values():
         v["frac"] = v["achieved"] / v["peak"]
-        v["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
+        if v["unit"] == "TFLOP/s":
+            mult = 2 if v is stages.get("indexer") and cfg.get("idx_dtype") == "fp8" else 1
+            v["frac_of_burst"] = v["achieved"] / (tflops * mult)
+            v["frac_of_sustained"] = v["achieved"] / (tf_sust * mult)
+            v["peak_source"] = tf_label + (" (MEASURED_PEAKS.json)" if src == "measured" else "")
+        else:
+            v["peak_source"] = "measured copy bandwidth (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
     if cfg.get("idx_dtype") == "fp8":
-        stages["indexer"]["peak_source"] += "; FP8 peak taken as 2x the measured sustained bf16 (none measured)"
+        stages["indexer"]["peak_source"] += "; FP8 peak taken as 2x the bf16 one (none measured)"
     if pipe.fused:
         elt = 2 if cfg["dtype"] == "bf16" else 4
         io = sum(x.numel() * x.element_size() for x in inputs[:4]) + B * T * cfg["HQ"] * cfg["D"] * 4
@@ -507,17 +606,28 @@ def run_b200(args, cfg, world, rank, local):
     # out.  As in a serving loop, steps are pipelined over two device buffer sets:
     # step i+1's host->device copies (copy-in stream) and step i-1's
     # device->host copy (copy-out stream) overlap step i's kernels.
+    # Each rank copies only its own query rows.  With several ranks sharing one
+    # sequence, the key side (k_idx, K, V) crosses PCIe once: every rank copies
+    # 1/N of its rows and one NCCL all_gather over NVLink assembles the rest.
     if not args.no_e2e:
         q, kk, w, Q, K, V = inputs
-        h_key = [x.cpu().pin_memory() for x in (kk, K, V)]
-        h_rows = [[x[:, b.start:b.stop].cpu().pin_memory() for x in (q, w, Q)] for b in blocks]
+        share_keys = args.scaling == "strong" and world > 1 and T % world == 0
+        key_full = [x for x in (kk, K, V)]
+        if share_keys:
+            rows_r = slice(rank * (T // world), (rank + 1) * (T // world))
+            h_key = [x[:, rows_r].cpu().pin_memory() for x in key_full]
+        else:
+            h_key = [x.cpu().pin_memory() for x in key_full]
+        h_rows = [[p[name].cpu().pin_memory() for name in ("q", "w", "Q")] for p in pipe.parts]
         NSLOT = 2
-        d_key = [[torch.empty_like(x, device=dev) for x in h_key] for _ in range(NSLOT)]
+        d_key = [[torch.empty_like(x, device=dev) for x in key_full] for _ in range(NSLOT)]
+        d_chunk = [[torch.empty_like(x, device=dev) for x in h_key] for _ in range(NSLOT)] if share_keys else None
         d_rows = [[[torch.empty_like(x, device=dev) for x in r] for r in h_rows] for _ in range(NSLOT)]
-        ws = [[torch.empty(forward_workspace_bytes(B, b.stop - b.start, T, cfg["k"]), device=dev,
-                           dtype=torch.uint8) for b in blocks] for _ in range(NSLOT)]
-        h_out = [[torch.empty((B, b.stop - b.start, cfg["HQ"], cfg["D"]), dtype=torch.float32).pin_memory()
-                  for b in blocks] for _ in range(NSLOT)]
+        ws = [[torch.empty(max(1, forward_workspace_bytes(p["NB"], p["Tq"], T, cfg["k"], cfg["HQ"], cfg["D"],
+                                                          Q.dtype)), device=dev, dtype=torch.uint8)
+               for p in pipe.parts] for _ in range(NSLOT)]
+        h_out = [[torch.empty(tuple(p["O"].shape), dtype=torch.float32).pin_memory() for p in pipe.parts]
+                 for _ in range(NSLOT)]
         bi = sum(x.numel() * x.element_size() for x in h_key) + \
             sum(x.numel() * x.element_size() for r in h_rows for x in r)
         bo = sum(x.numel() * x.element_size() for x in h_out[0])
@@ -526,24 +636,32 @@ def run_b200(args, cfg, world, rank, local):
         comp_done = [ev() for _ in range(NSLOT)]
         in_done = [ev() for _ in range(NSLOT)]
         used = [False] * NSLOT
+        if share_keys:
+            import torch.distributed as dist
 
         def e2e_step(i):
             sl = i % NSLOT
             with torch.cuda.stream(s_in):
                 if used[sl]:
                     s_in.wait_event(comp_done[sl])   # the slot's previous step has read its inputs
-                for d, h in zip(d_key[sl], h_key):
-                    d.copy_(h, non_blocking=True)
+                if share_keys:
+                    for c, h, full in zip(d_chunk[sl], h_key, d_key[sl]):
+                        c.copy_(h, non_blocking=True)
+                        # [1, T, ...] from N chunks of [1, T/N, ...] (dimension 0 of the flat views)
+                        dist.all_gather_into_tensor(full.view(T, -1), c.view(T // world, -1))
+                else:
+                    for d, h in zip(d_key[sl], h_key):
+                        d.copy_(h, non_blocking=True)
                 for dr, hr in zip(d_rows[sl], h_rows):
                     for d, h in zip(dr, hr):
                         d.copy_(h, non_blocking=True)
                 in_done[sl].record(s_in)
             stream.wait_event(in_done[sl])
             outs = []
-            for j, b in enumerate(blocks):
-                outs.append(dsa_forward(d_rows[sl][j][0], d_key[sl][0], d_rows[sl][j][1], d_rows[sl][j][2],
-                                        d_key[sl][1], d_key[sl][2], cfg["k"], q_row0=b.start,
-                                        workspace=ws[sl][j]))
+            for j, p in enumerate(pipe.parts):
+                qd, wd, Qd = d_rows[sl][j]
+                outs.append(dsa_forward(qd, d_key[sl][0], wd, Qd, d_key[sl][1], d_key[sl][2], cfg["k"],
+                                        q_row0=p["q0"], row_bstep=p["bstep"], workspace=ws[sl][j]))
             comp_done[sl].record(stream)
             used[sl] = True
             with torch.cuda.stream(s_out):
@@ -554,8 +672,8 @@ def run_b200(args, cfg, world, rank, local):
 
         for i in range(max(1, args.warmup)):
             e2e_step(i)
-        barrier(world)
         s_in.synchronize(); s_out.synchronize()
+        barrier(world)
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(s_in)
         stream.wait_event(e_start)
@@ -566,35 +684,40 @@ def run_b200(args, cfg, world, rank, local):
         e_end.synchronize()
         barrier(world)
         e_ms = max_over_ranks(e_start.elapsed_time(e_end), world) / args.steps
+        h2d = max_over_ranks(float(bi), world) if world > 1 else bi
         line["e2e"] = {"value": tokens / (e_ms / 1e3), "unit": "query-tokens/s", "ms_per_step": e_ms,
-                       "h2d_bytes_per_step": bi * world, "d2h_bytes_per_step": bo * world,
-                       "api": "dsa_attention.dsa_forward (C ABI dsa_forward), pinned host buffers, "
-                              "copies of neighbouring steps overlapped on two streams"}
-        line["gpu_launches"] += 3 * len(blocks) * args.steps
-        del h_key, h_rows, d_key, d_rows, ws, h_out
+                       "h2d_bytes_per_step": sum_over_ranks(bi, world),
+                       "d2h_bytes_per_step": sum_over_ranks(bo, world),
+                       "h2d_bytes_per_step_max_rank": h2d,
+                       "api": "dsa_attention.dsa_forward (C ABI dsa_forward_ex), pinned host buffers, "
+                              "copies of neighbouring steps overlapped on two streams" +
+                              ("; key side copied 1/N per rank and all-gathered over NVLink (NCCL) "
+                               "before the forward" if share_keys else "")}
+        line["gpu_launches"] += pipe.launches_per_step * args.steps
+        del h_key, h_rows, d_key, d_rows, ws, h_out, d_chunk
 
     # ---- verification (outside every timed region): gather the sharded rows over
     # NCCL and compare them with rank 0's own single-GPU forward of the whole
     # workload.  Both run the same kernels, so the rows must match bit for bit.
-    if args.verify and args.scaling == "strong":
+    if args.scaling == "strong" and not args.no_verify:
         from dsa_attention import dsa_forward as fwd_all
-        plan = sharding.zigzag_plan(T, world)
-        local_rows = torch.cat([p["O"] for p in pipe.parts], dim=1)
+        plan = [blocks] if world == 1 else sharding.zigzag_plan(T, world)
+        local_rows = pipe.out_rows()
         full = sharding.gather_rows(local_rows, plan) if world > 1 else local_rows
         if rank == 0:
             whole = fwd_all(*inputs, cfg["k"])
             line["verify"] = {"rows": T, "max_abs_diff": float((full - whole).abs().max()),
                               "bitwise_equal": bool(torch.equal(full, whole)),
                               "gather": "NCCL all_gather of output rows" if world > 1 else "none (1 rank)"}
-    elif args.verify:
-        line["verify"] = {"skipped": "weak scaling: every rank computes whole sequences itself"}
+        del full
 
     # ---- CPU baseline (rank 0 at N=1 only)
     if world == 1 and rank == 0 and not args.no_cpu:
         ctx = cpu_reference_setup(cfg, inputs)
         rate, rows, el = cpu_reference_rate(ctx, cfg, args.cpu_seconds, CHUNK[args.config])
         line["cpu_baseline"] = {"value": rate, "unit": "query-tokens/s", "cores": ctx["threads"],
-                                "kind": cpu_kind(ctx), "sample": cpu_sample_text(ctx, cfg, rows, el)}
+                                "kind": cpu_kind(ctx), "sample": cpu_sample_text(ctx, cfg, rows, el),
+                                **cpu_extra(ctx, cfg, rows)}
     return line
 
 
@@ -690,7 +813,8 @@ def run_reference(args, cfg, world, rank, local):
     line["cpu_baseline"] = {"value": value, "unit": "query-tokens/s", "cores": ctx["threads"],
                             "kind": cpu_kind(ctx),
                             "sample": cpu_sample_text(ctx, cfg, step_rows * args.steps, el) +
-                            f"; {step_rows} rows per step"}
+                            f"; {step_rows} rows per step",
+                            **cpu_extra(ctx, cfg, step_rows * args.steps)}
     line["e2e"] = {"value": value, "unit": "query-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     line["gpu_launches"] = 0
     return line
@@ -703,17 +827,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c5", choices=sorted(CONFIGS) + ["c2"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--scaling", default="auto", choices=["auto", "weak", "strong"],
+                    help="auto: strong (one sequence's query rows split zig-zag over the ranks) when the "
+                         "config has one sequence (c5) or fewer sequences than ranks, else weak")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-step-seconds", type=float, default=3.0)
-    ap.add_argument("--verify", action="store_true",
-                    help="after timing, gather the sharded output rows (NCCL) and compare with a "
-                         "single-GPU forward on rank 0 (strong scaling)")
+    ap.add_argument("--no-verify", action="store_true",
+                    help="skip the check after timing (strong scaling): gather the sharded output rows "
+                         "(NCCL) and compare them with a single-GPU forward on rank 0")
     args = ap.parse_args()
     cfg = CONFIGS.get(args.config)
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.scaling == "auto":
+        args.scaling = "strong" if cfg is not None and (cfg["B"] == 1 or cfg["B"] < world) else "weak"
     if args.config == "c2":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "c2 is a top-K-only config; its CPU "

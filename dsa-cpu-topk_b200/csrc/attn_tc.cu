@@ -62,6 +62,8 @@ struct AtParams {
     const uint32_t* bits;
     int64_t words;        // bitmap words per query row (multiple of 4)
     int64_t T_q, T_k, q_row0;
+    int64_t row_bstep;    // batch b's query rows start at q_row0 + b*row_bstep
+    int kshared, vshared; // K / V have batch stride 0: every batch reads batch 0
     int B, HQ, D;
     int n_qt, nkb, total_units;
     int nK, nV, nP;
@@ -69,6 +71,9 @@ struct AtParams {
     float sl2;            // scale * log2(e)
     int stall;            // test hook: the producer issues no loads, so every wait times out
     int o_vec8;           // O 32-byte aligned: 256-bit output stores
+    const float* vscale;  // V was converted to fp16 as V / *vscale (power of two); O is scaled back
+    const uint32_t* summ; // per (batch, query tile): one bit per key block holding any kept key, or null
+    int sw;               // summary words per query tile
     unsigned long long timeout_ns;
 };
 
@@ -87,7 +92,7 @@ __device__ __forceinline__ Unit decode_unit(int u, const AtParams& p) {
     r.h = rem - r.b * p.HQ;
     int64_t tq_end = (int64_t)(r.qt + 1) * BM;
     if (tq_end > p.T_q) tq_end = p.T_q;
-    int64_t nb = (p.q_row0 + tq_end - 1) / BN + 1;
+    int64_t nb = (p.q_row0 + r.b * p.row_bstep + tq_end - 1) / BN + 1;
     if (nb > p.nkb) nb = p.nkb;
     r.nblk = (int)nb;
     return r;
@@ -102,7 +107,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <bool F16>
+template <bool F16, bool PV16>
 __global__ void __launch_bounds__(NTHREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                    const __grid_constant__ CUtensorMap tmv, const AtParams p) {
@@ -184,7 +189,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         mbar_expect_tx(&k_full[ks], p.kv_bytes);
                         for (int c = 0; c < nch; ++c)
                             tma_load_4d(sK + (size_t)ks * p.kv_bytes + c * BN * 128, &tmk, &k_full[ks],
-                                        c * 64, w.h, j * BN, w.b);
+                                        c * 64, w.h, j * BN, p.kshared ? 0 : w.b);
                     }
                     if (++ks == p.nK) { ks = 0; kph ^= 1; }
                     if (!(ok = mbar_wait(&v_empty[vs], vph ^ 1, &s_abort, p.timeout_ns, flag))) break;
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         mbar_expect_tx(&v_full[vs], p.kv_bytes);
                         for (int c = 0; c < nch; ++c)
                             tma_load_4d(sV + (size_t)vs * p.kv_bytes + c * BN * 128, &tmv, &v_full[vs],
-                                        c * 64, w.h, j * BN, w.b);
+                                        c * 64, w.h, j * BN, p.vshared ? 0 : w.b);
                     }
                     if (++vs == p.nV) { vs = 0; vph ^= 1; }
                 }
@@ -206,7 +211,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t fmt = F16 ? 0u : 1u;
             const uint32_t idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                                      ((uint32_t)(BM >> 4) << 24);
-            const uint32_t idesc_o = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) |
+            const uint32_t fmt_o = PV16 ? 0u : 1u;   // P and V: fp16 or bf16
+            const uint32_t idesc_o = (1u << 4) | (fmt_o << 7) | (fmt_o << 10) | (1u << 16) |
                                      ((uint32_t)(p.D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
             const uint32_t sq = smem_u32(sQ);
             int ks = 0, vs = 0;
@@ -356,10 +362,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             lp[e] += pv[e];
                         }
                         uint4 pk;
-                        pk.x = pack2(pv[0], pv[1], F16);
-                        pk.y = pack2(pv[2], pv[3], F16);
-                        pk.z = pack2(pv[4], pv[5], F16);
-                        pk.w = pack2(pv[6], pv[7], F16);
+                        pk.x = pack2(pv[0], pv[1], PV16);
+                        pk.y = pack2(pv[2], pv[3], PV16);
+                        pk.z = pack2(pv[4], pv[5], PV16);
+                        pk.w = pack2(pv[6], pv[7], PV16);
                         *reinterpret_cast<uint4*>(prow + cc * BM * 128 + ((i ^ (row & 7)) << 4)) = pk;
                     }
                 }
@@ -376,7 +382,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!(ok = wait_all(&pv_done[g1 & 1], (g1 >> 1) & 1))) break;
             }
             tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
+            // an empty kept set (a NaN threshold) gives NaN, as the reference's
+            // softmax over all -inf logits does
+            const float inv = (l > 0.f ? 1.f / l : __uint_as_float(0x7fc00000u)) *
+                              (p.vscale ? __ldg(p.vscale) : 1.f);
             float* orow = p.O + (((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.HQ + w.h) * p.D;
             for (int c = 0; c < p.D / 32; ++c) {
                 uint32_t o[32];
@@ -432,10 +441,10 @@ struct Unit2 {
     int b, h, qa, na, nb;   // tile A = qa, tile B = qa + 1 (nb = 0: no tile B)
 };
 
-__device__ __forceinline__ int tile_blocks(int qt, const AtParams& p) {
+__device__ __forceinline__ int tile_blocks(int qt, int b, const AtParams& p) {
     int64_t tq_end = (int64_t)(qt + 1) * BM;
     if (tq_end > p.T_q) tq_end = p.T_q;
-    int64_t nb = (p.q_row0 + tq_end - 1) / BN + 1;
+    int64_t nb = (p.q_row0 + b * p.row_bstep + tq_end - 1) / BN + 1;
     if (nb > p.nkb) nb = p.nkb;
     return (int)nb;
 }
@@ -450,12 +459,17 @@ __device__ __forceinline__ Unit2 decode_unit2(int u, const AtParams& p) {
     r.b = rem / p.HQ;
     r.h = rem - r.b * p.HQ;
     r.qa = 2 * m;
-    r.na = tile_blocks(r.qa, p);
-    r.nb = r.qa + 1 < p.n_qt ? tile_blocks(r.qa + 1, p) : 0;
+    r.na = tile_blocks(r.qa, r.b, p);
+    r.nb = r.qa + 1 < p.n_qt ? tile_blocks(r.qa + 1, r.b, p) : 0;
     return r;
 }
 
-template <bool F16>
+// Whether key block j holds a kept key of query tile qt (always, without a summary).
+__device__ __forceinline__ bool block_used(const AtParams& p, int b, int qt, int j) {
+    return !p.summ || ((__ldg(p.summ + ((int64_t)b * p.n_qt + qt) * p.sw + (j >> 5)) >> (j & 31)) & 1u);
+}
+
+template <bool F16, bool PV16>
 __global__ void __launch_bounds__(NT2, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                     const __grid_constant__ CUtensorMap tmv, const AtParams p) {
@@ -545,22 +559,32 @@ __global__ void __launch_bounds__(NT2, 1)
                         mbar_expect_tx(&k_full[ks], p.kv_bytes);
                         for (int c = 0; c < nch; ++c)
                             tma_load_4d(sK + (size_t)ks * p.kv_bytes + c * BN * 128, &tmk, &k_full[ks],
-                                        c * 64, w.h, jb * BN, w.b);
+                                        c * 64, w.h, jb * BN, p.kshared ? 0 : w.b);
                     }
                     if (++ks == p.nK) { ks = 0; kph ^= 1; }
                     return true;
                 };
-                if (!(ok = load_k(0))) break;
-                for (int j = 0; j < nblk; ++j) {
-                    if (j + 1 < nblk && !(ok = load_k(j + 1))) break;
+                // the unit's key blocks: those either tile uses (all causal ones
+                // without a summary); K runs one used block ahead of V
+                auto next_used = [&](int j) {
+                    do { ++j; } while (j < nblk && !((j < w.na && block_used(p, w.b, w.qa, j)) ||
+                                                     (j < w.nb && block_used(p, w.b, w.qa + 1, j))));
+                    return j;
+                };
+                int j = next_used(-1);
+                if (j < nblk && !(ok = load_k(j))) break;
+                for (; j < nblk;) {
+                    const int jn = next_used(j);
+                    if (jn < nblk && !(ok = load_k(jn))) break;
                     if (!(ok = mbar_wait(&v_empty[vs], vph ^ 1, &s_abort, p.timeout_ns, flag))) break;
                     if (!p.stall) {
                         mbar_expect_tx(&v_full[vs], p.kv_bytes);
                         for (int c = 0; c < nch; ++c)
                             tma_load_4d(sV + (size_t)vs * p.kv_bytes + c * BN * 128, &tmv, &v_full[vs],
-                                        c * 64, w.h, j * BN, w.b);
+                                        c * 64, w.h, j * BN, p.vshared ? 0 : w.b);
                     }
                     if (++vs == p.nV) { vs = 0; vph ^= 1; }
+                    j = jn;
                 }
             }
         } else if ((warp == 1 || warp == 2) && lane == 0) {
@@ -575,7 +599,8 @@ __global__ void __launch_bounds__(NT2, 1)
             const uint32_t fmt = F16 ? 0u : 1u;
             const uint32_t idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
                                      ((uint32_t)(BM >> 4) << 24);
-            const uint32_t idesc_o = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) |
+            const uint32_t fmt_o = PV16 ? 0u : 1u;   // P and V: fp16 or bf16
+            const uint32_t idesc_o = (1u << 4) | (fmt_o << 7) | (fmt_o << 10) | (1u << 16) |
                                      ((uint32_t)(p.D >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
             const uint32_t qb = smem_u32(sQ + (size_t)x * p.q_bytes);
             const uint32_t s_tm = tmem_base + (uint32_t)x * 256u;
@@ -605,7 +630,7 @@ __global__ void __launch_bounds__(NT2, 1)
                 return true;
             };
             // O (+)= P V, V from the current V stage
-            auto issue_pv = [&](int j) -> bool {
+            auto issue_pv = [&](bool first) -> bool {
                 if (!mbar_wait(&v_full[vs], vph, &s_abort, p.timeout_ns, flag)) return false;
                 if (!mbar_wait(&p_full[x], GP & 1, &s_abort, p.timeout_ns, flag)) return false;
                 tc_fence_after();
@@ -613,7 +638,7 @@ __global__ void __launch_bounds__(NT2, 1)
 #pragma unroll
                 for (int kb = 0; kb < BN / 16; ++kb)
                     umma<false>(o_tm, sw128_desc(pa + (kb >> 2) * BM * 128 + (kb & 3) * 32),
-                                sw128_desc_mn(vb + kb * 16 * 128, BN * 128), idesc_o, (j | kb) != 0);
+                                sw128_desc_mn(vb + kb * 16 * 128, BN * 128), idesc_o, !first || kb != 0);
                 umma_commit(&pv_done[x]);
                 umma_commit(&v_empty[vs]);
                 ++GP;
@@ -632,22 +657,48 @@ __global__ void __launch_bounds__(NT2, 1)
                 const int nblk = w.nb > w.na ? w.nb : w.na;
                 if (!(ok = mbar_wait(q_full, qph, &s_abort, p.timeout_ns, flag))) break;
                 qph ^= 1;
-                if (n == 0) mbar_arrive(q_empty);
-                else if (!(ok = issue_s())) break;
-                if (n == 1) umma_commit(q_empty);
-                for (int j = 0; ok && j < n; ++j) {
-                    if (j + 1 < n) {
-                        if (!(ok = issue_s())) break;
-                        if (j + 2 == n) umma_commit(q_empty);   // this tile's last S was issued
+                // The stages arrive in the producer's order K(u0), then K(u_i+1)
+                // before V(u_i) over the unit's used blocks u_i; they are taken in
+                // that order.  A block of this tile gets its S (on K) and PV (on
+                // V) MMA; a block only the other tile uses is released.
+                auto mine = [&](int j) { return j < n && block_used(p, w.b, w.qa + x, j); };
+                auto next_used = [&](int j) {
+                    do { ++j; } while (j < nblk && !((j < w.na && block_used(p, w.b, w.qa, j)) ||
+                                                     (j < w.nb && block_used(p, w.b, w.qa + 1, j))));
+                    return j;
+                };
+                int last = -1;   // this tile's last block: Q is free once its S is issued
+                for (int j = n - 1; j >= 0 && last < 0; --j)
+                    if (mine(j)) last = j;
+                if (last < 0) mbar_arrive(q_empty);
+                bool first = true;
+                auto take_k = [&](int j) -> bool {
+                    if (mine(j)) {
+                        if (!issue_s()) return false;
+                        if (j == last) umma_commit(q_empty);
+                        return true;
                     }
-                    if (!(ok = issue_pv(j))) break;
-                }
-                // blocks of this unit that only the other tile uses (K loads run one ahead of V)
-                for (int j = n; ok && j < nblk; ++j) {
-                    if (!(ok = skip_stage(k_full, k_empty, ks, kph))) break;
+                    if (!skip_stage(k_full, k_empty, ks, kph)) return false;
                     k_next();
-                    if (!(ok = skip_stage(v_full, v_empty, vs, vph))) break;
+                    return true;
+                };
+                auto take_v = [&](int j) -> bool {
+                    if (mine(j)) {
+                        if (!issue_pv(first)) return false;
+                        first = false;
+                        return true;
+                    }
+                    if (!skip_stage(v_full, v_empty, vs, vph)) return false;
                     v_next();
+                    return true;
+                };
+                int j = next_used(-1);
+                if (j < nblk && !(ok = take_k(j))) break;
+                while (j < nblk) {
+                    const int jn = next_used(j);
+                    if (jn < nblk && !(ok = take_k(jn))) break;
+                    if (!(ok = take_v(j))) break;
+                    j = jn;
                 }
             }
         }
@@ -676,8 +727,15 @@ __global__ void __launch_bounds__(NT2, 1)
             const bool row_ok = tq < p.T_q;
             const uint32_t* brow = p.bits + ((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.words;
             float m_run = kNegInf, l = 0.f;
-            uint4 mk = row_ok ? __ldg(reinterpret_cast<const uint4*>(brow)) : make_uint4(0, 0, 0, 0);
-            for (int j = 0; j < nblk; ++j, ++G) {
+            // this tile's key blocks (those holding a kept key of the tile)
+            auto next_mine = [&](int j) {
+                do { ++j; } while (j < nblk && !block_used(p, w.b, qt, j));
+                return j;
+            };
+            int j = next_mine(-1);
+            uint4 mk = row_ok && j < nblk ? __ldg(reinterpret_cast<const uint4*>(brow) + j) : make_uint4(0, 0, 0, 0);
+            int jj = 0;   // ordinal of block j among the tile's blocks
+            for (; j < nblk; ++jj, ++G) {
                 if (!(ok = wait_all(&s_full[x], G & 1))) break;
                 tc_fence_after();
                 uint32_t s[128];
@@ -690,7 +748,9 @@ __global__ void __launch_bounds__(NT2, 1)
                 if (lane == 0) mbar_arrive(&s_free[x]);   // the MMA may write S_X(j+1)
 
                 const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
-                if (row_ok && j + 1 < nblk) mk = __ldg(reinterpret_cast<const uint4*>(brow) + j + 1);
+                const int jn = next_mine(j);
+                if (row_ok && jn < nblk) mk = __ldg(reinterpret_cast<const uint4*>(brow) + jn);
+                j = jn;
                 // dropped logits -> -inf; row max of the kept ones (8 chains of 3-input max)
                 float mxp[8];
 #pragma unroll
@@ -715,7 +775,7 @@ __global__ void __launch_bounds__(NT2, 1)
                     l *= alpha;
                 }
                 // P_X's buffer and O_X: PV_X(j-1) must have landed
-                if (j > 0 && !(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
+                if (jj > 0 && !(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
                 // P = 2^(x*sl2 - m): the exponent in fp32 (packed FMA), 2^ in fp32
                 // on the MUFU, rounded to the 16-bit input type for the PV product;
                 // l sums the fp32 values (packed adds).  16-byte slot i of the
@@ -733,7 +793,7 @@ __global__ void __launch_bounds__(NT2, 1)
                             const int c = cc * 64 + i * 8 + 2 * e;
                             const float2 xx =
                                 fma2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2v, nmu);
-                            pk[e] = ex2_pair_sum<F16>(xx.x, xx.y, lp[e]);
+                            pk[e] = ex2_pair_sum<PV16>(xx.x, xx.y, lp[e]);
                         }
                         *reinterpret_cast<uint4*>(prow_base + cc * BM * 128 + ((i ^ (row & 7)) << 4)) =
                             make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -750,7 +810,7 @@ __global__ void __launch_bounds__(NT2, 1)
                 }
                 // rescale O_X (after the row's S values are dead); PV_X(j) is
                 // issued only after p_full, so it sees the rescaled O
-                if (j > 0 && __any_sync(0xffffffffu, need)) {
+                if (jj > 0 && __any_sync(0xffffffffu, need)) {
                     tc_fence_after();
                     for (int c = 0; c < p.D / 32; ++c) {
                         uint32_t o[32];
@@ -768,9 +828,21 @@ __global__ void __launch_bounds__(NT2, 1)
                 if (lane == 0) mbar_arrive(&p_full[x]);
             }
             if (!ok) break;
+            if (jj == 0) {
+                // no key block of this tile holds a kept key: every row's kept set
+                // is empty (NaN thresholds), and so is its output (NaN, as the
+                // reference's softmax over all -inf logits)
+                float* orow = p.O + (((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.HQ + w.h) * p.D;
+                if (row_ok)
+                    for (int c = 0; c < p.D; ++c) orow[c] = __uint_as_float(0x7fc00000u);
+                continue;
+            }
             if (!(ok = wait_all(&pv_done[x], (G - 1) & 1))) break;
             tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
+            // an empty kept set (a NaN threshold) gives NaN, as the reference's
+            // softmax over all -inf logits does
+            const float inv = (l > 0.f ? 1.f / l : __uint_as_float(0x7fc00000u)) *
+                              (p.vscale ? __ldg(p.vscale) : 1.f);
             float* orow = p.O + (((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.HQ + w.h) * p.D;
             for (int c = 0; c < p.D / 32; ++c) {
                 uint32_t o[32];
@@ -809,15 +881,16 @@ __global__ void __launch_bounds__(NT2, 1)
 }
 
 // Kept-set bitmap: bit (s & 31) of word s/32 of query row r is set iff
-// s <= q_row0 + r % T_q and scores[r, s] >= thr[r].  One CTA per query row;
+// s <= q_row0 + (r / T_q)*row_bstep + r % T_q and scores[r, s] >= thr[r].  One CTA per query row;
 // each warp turns 32 consecutive scores into one word with a ballot.  Words
 // past the causal end (up to `words`) are written as zero.
 __global__ void __launch_bounds__(256) kept_bitmap_kernel(const float* __restrict__ scores,
                                                           const float* __restrict__ thr,
                                                           uint32_t* __restrict__ bits, int64_t T_q,
-                                                          int64_t T_k, int64_t q_row0, int64_t words) {
+                                                          int64_t T_k, int64_t q_row0, int64_t words,
+                                                          int64_t row_bstep) {
     const int64_t row = blockIdx.x;
-    int64_t last = q_row0 + row % T_q;   // last causal key
+    int64_t last = q_row0 + (row / T_q) * row_bstep + row % T_q;   // last causal key
     if (last > T_k - 1) last = T_k - 1;
     const float th = thr[row];
     const float* srow = scores + row * T_k;
@@ -832,12 +905,118 @@ __global__ void __launch_bounds__(256) kept_bitmap_kernel(const float* __restric
     }
 }
 
+// ---- V in fp16 for the P.V product ------------------------------------------
+// With bf16 inputs the softmax weights P would enter the P.V MMA as bf16 (an
+// 8-bit significand: up to 2^-9 relative error per weight).  One MMA takes one
+// operand type, so P in fp16 (11 bits, 8x finer) needs V in fp16 too: V is
+// copied once per call as fp16(V / s), s a power of two with max|V| / s <=
+// 2^15 (exact scaling; every bf16 value in that range is exact in fp16), and
+// the output is multiplied back by s.  Non-finite V keeps s = 1.
+
+// max |V| as float bits (non-negative floats order like their bit patterns;
+// NaN's bits exceed +inf's).  V rows of D elements at b*sb + t*sr + h*sh.
+__global__ void __launch_bounds__(256) v_absmax_kernel(const __nv_bfloat16* __restrict__ V, int64_t T_k,
+                                                       int HQ, int D, int64_t sb, int64_t sr, int64_t sh,
+                                                       int64_t chunks, uint32_t* __restrict__ amax) {
+    const int cpr = D / 8;   // 16-byte chunks per row
+    uint32_t m = 0;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < chunks;
+         c += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = c / cpr;
+        const int off = (int)(c - row * cpr) * 8;
+        const int h = (int)(row % HQ);
+        const int64_t bt = row / HQ;
+        const int64_t t = bt % T_k, b = bt / T_k;
+        const uint4 v = ldg16(V + b * sb + t * sr + h * sh + off);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = (w[i] << 16) & 0x7fffffffu, hi = w[i] & 0x7fff0000u;
+            m = max(m, max(lo, hi));
+        }
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    if ((threadIdx.x & 31) == 0 && m) atomicMax(amax, m);
+}
+
+__global__ void __launch_bounds__(256) v_to_f16_kernel(const __nv_bfloat16* __restrict__ V, int64_t T_k,
+                                                       int HQ, int D, int64_t sb, int64_t sr, int64_t sh,
+                                                       int64_t chunks, const uint32_t* __restrict__ amax,
+                                                       __half* __restrict__ out, float* __restrict__ scale) {
+    const float a = __uint_as_float(*amax);
+    float s = 1.f;
+    if (a <= 3.4028234663852886e38f)           // finite: smallest power of two with a / s <= 2^15
+        while (a > 32768.f * s) s *= 2.f;
+    const float inv = 1.f / s;                 // a power of two: exact
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale = s;
+    const int cpr = D / 8;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < chunks;
+         c += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = c / cpr;
+        const int off = (int)(c - row * cpr) * 8;
+        const int h = (int)(row % HQ);
+        const int64_t bt = row / HQ;
+        const int64_t t = bt % T_k, b = bt / T_k;
+        const uint4 v = ldg16(V + b * sb + t * sr + h * sh + off);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 hv = __floats2half2_rn(__uint_as_float(w[i] << 16) * inv,
+                                                 __uint_as_float(w[i] & 0xffff0000u) * inv);
+            o[i] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(out + row * D + off) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Block summary of the kept-set bitmap: bit j of word (b*n_qt + qt)*sw + j/32
+// is set iff key block j holds a kept key of some row of query tile qt.  One
+// CTA per (query tile, batch); thread t ORs key block t (t + 256, ...) over
+// the tile's rows, each row's block read as one 16-byte load.
+__global__ void __launch_bounds__(256) block_summary_kernel(const uint32_t* __restrict__ bits, int64_t words,
+                                                            int64_t T_q, int n_qt, int nkb, int sw,
+                                                            uint32_t* __restrict__ summ) {
+    const int qt = blockIdx.x, b = blockIdx.y;
+    const int64_t r0 = (int64_t)qt * BM;
+    const int nr = (int)(T_q - r0 < BM ? T_q - r0 : BM);
+    const uint32_t* tile = bits + ((int64_t)b * T_q + r0) * words;
+    uint32_t* out = summ + ((int64_t)b * n_qt + qt) * sw;
+    for (int j0 = 0; j0 < sw * 32; j0 += blockDim.x) {
+        const int j = j0 + threadIdx.x;
+        uint32_t any = 0;
+        if (j < nkb) {
+            const uint4* col = reinterpret_cast<const uint4*>(tile) + j;
+            const int64_t stride = words / 4;
+#pragma unroll 8
+            for (int r = 0; r < nr; ++r) {
+                const uint4 v = __ldg(col + r * stride);
+                any |= v.x | v.y | v.z | v.w;
+            }
+        }
+        const uint32_t m = __ballot_sync(0xffffffffu, any != 0);
+        if ((threadIdx.x & 31) == 0 && j < sw * 32) out[j >> 5] = m;
+    }
+}
+
 }  // namespace
+
+// Workspace of dsa_sparse_attn_bitmap_ex: a 256-byte header (max |V|, the V
+// scale), the block summary [B, n_qt, ceil(nkb/32)] uint32 (256-byte
+// aligned), and for bf16 inputs the fp16 copy of V [B, T_k, HQ, D].
+static size_t summ_bytes(int64_t B, int64_t T_q, int64_t T_k) {
+    const int64_t n_qt = (T_q + BM - 1) / BM, nkb = (T_k + BN - 1) / BN;
+    return (((size_t)B * n_qt * ((nkb + 31) / 32) * 4) + 255) & ~size_t(255);
+}
+size_t attn_ws_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t HQ, int64_t D, int dtype) {
+    return 256 + summ_bytes(B, T_q, T_k) +
+           (dtype == DSA_BF16 ? (size_t)B * (size_t)T_k * (size_t)HQ * (size_t)D * 2 : 0);
+}
 
 int64_t bitmap_words(int64_t T_k) { return ((T_k + BN - 1) / BN) * (BN / 32); }
 
 int kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B, int64_t T_q,
-                int64_t T_k, int64_t q_row0, int64_t words, cudaStream_t stream) {
+                int64_t T_k, int64_t q_row0, int64_t words, int64_t row_bstep, cudaStream_t stream) {
     if (!scores || !thr || !bits) return fail(DSA_ERR_INVALID, "kept_bitmap: null pointer");
     if (B < 0 || T_q < 0 || T_k < 1 || q_row0 < 0)
         return fail(DSA_ERR_INVALID, "kept_bitmap: bad sizes");
@@ -847,7 +1026,8 @@ int kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B
     const int64_t rows = B * T_q;
     if (rows == 0) return DSA_OK;
     if (rows > INT32_MAX) return fail(DSA_ERR_INVALID, "kept_bitmap: too many rows");
-    kept_bitmap_kernel<<<(unsigned)rows, 256, 0, stream>>>(scores, thr, bits, T_q, T_k, q_row0, words);
+    kept_bitmap_kernel<<<(unsigned)rows, 256, 0, stream>>>(scores, thr, bits, T_q, T_k, q_row0, words,
+                                                           row_bstep);
     return check_launch("kept_bitmap_kernel");
 }
 
@@ -872,9 +1052,16 @@ bool attn_tc_supported(int64_t HQ, int64_t DQ, int64_t DV, int dtype) {
 // uses the gather kernel instead).
 int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, const void* V,
             float* O, int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t D,
-            float scale, int dtype, cudaStream_t stream) {
+            float scale, int dtype, const dsa_layout& L, void* ws, size_t ws_bytes, cudaStream_t stream) {
     if (!attn_tc_supported(HQ, D, D, dtype)) return -100;
     if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(bits))
+        return -100;
+    // tensor-map strides: positive multiples of 16 bytes; a K or V batch
+    // stride of 0 is read as one shared batch
+    for (int i = 1; i < 3; ++i)
+        if (!tma_stride_ok(L.Q[i], 2) || !tma_stride_ok(L.K[i], 2) || !tma_stride_ok(L.V[i], 2)) return -100;
+    if (B > 1 && (!tma_stride_ok(L.Q[0], 2) || (L.K[0] != 0 && !tma_stride_ok(L.K[0], 2)) ||
+                  (L.V[0] != 0 && !tma_stride_ok(L.V[0], 2))))
         return -100;
     AtParams p;
     p.O = O;
@@ -883,6 +1070,9 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
     p.T_q = T_q;
     p.T_k = T_k;
     p.q_row0 = q_row0;
+    p.row_bstep = L.row_bstep;
+    p.kshared = (B > 1 && L.K[0] == 0) ? 1 : 0;
+    p.vshared = (B > 1 && L.V[0] == 0) ? 1 : 0;
     p.B = (int)B;
     p.HQ = (int)HQ;
     p.D = (int)D;
@@ -899,6 +1089,20 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
     p.stall = getenv("DSA_TEST_ATTN_STALL") ? 1 : 0;
     p.timeout_ns = p.stall ? 20000000ull : 2000000000ull;
     p.o_vec8 = (reinterpret_cast<uintptr_t>(O) & 31u) == 0 ? 1 : 0;
+    p.vscale = nullptr;
+    p.summ = nullptr;
+    p.sw = (p.nkb + 31) / 32;
+    // with a workspace: the block summary (key blocks no row of a query tile
+    // keeps are skipped), and for bf16 inputs the fp16 copy of V (P.V in fp16,
+    // see v_to_f16_kernel)
+    const int64_t B_v = p.vshared ? 1 : B;
+    const size_t sbytes = summ_bytes(B, T_q, T_k);
+    const bool have_ws = ws && (reinterpret_cast<uintptr_t>(ws) & 255u) == 0 && ws_bytes >= 256 + sbytes;
+    const bool v16 = dtype == DSA_BF16 && have_ws &&
+                     ws_bytes >= 256 + sbytes + (size_t)B_v * T_k * HQ * D * 2;
+    const bool pv16 = dtype == DSA_F16 || v16;
+    // DSA_ATTN_NO_SKIP=1: process every causal key block (cross-check of the skipping)
+    const bool skip = have_ws && !getenv("DSA_ATTN_NO_SKIP");
     if (units == 0) return DSA_OK;
 
     int dev = 0, optin = 0;
@@ -907,8 +1111,12 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
         return fail(DSA_ERR_CUDA, "attn_tc: cannot query shared memory limits");
     // The two-tile kernel redistributes a launch pool of exactly 384 x 168
     // registers; it runs only when the compiled kernel asks for that many.
-    auto kern2 = dtype == DSA_F16 ? attn_tc2_kernel<true> : attn_tc2_kernel<false>;
-    auto kern1 = dtype == DSA_F16 ? attn_tc_kernel<true> : attn_tc_kernel<false>;
+    auto kern2 = dtype == DSA_F16 ? attn_tc2_kernel<true, true>
+                 : pv16          ? attn_tc2_kernel<false, true>
+                                 : attn_tc2_kernel<false, false>;
+    auto kern1 = dtype == DSA_F16 ? attn_tc_kernel<true, true>
+                 : pv16          ? attn_tc_kernel<false, true>
+                                 : attn_tc_kernel<false, false>;
     cudaFuncAttributes fa2, fa1;
     if (cudaFuncGetAttributes(&fa2, kern2) != cudaSuccess || cudaFuncGetAttributes(&fa1, kern1) != cudaSuccess)
         return fail(DSA_ERR_CUDA, "attn_tc: cannot query kernel attributes");
@@ -959,19 +1167,59 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
     const cuuint32_t box[4] = {64, 1, 128, 1};
     {
         const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)HQ, (cuuint64_t)T_q, (cuuint64_t)B};
-        const cuuint64_t str[3] = {(cuuint64_t)D * 2, (cuuint64_t)(HQ * D * 2),
-                                   (cuuint64_t)(T_q * HQ * D * 2)};
+        const cuuint64_t str[3] = {(cuuint64_t)L.Q[2] * 2, (cuuint64_t)L.Q[1] * 2,
+                                   (cuuint64_t)(B > 1 ? L.Q[0] : L.Q[1] * T_q) * 2};
         int rc = encode_map(&tmq, Q, 4, dims, str, box, "attn_tc: Q", dt);
         if (rc) return rc;
     }
+    const void* Vsrc = V;
+    int64_t vst[3] = {L.V[0], L.V[1], L.V[2]};
+    if (v16) {
+        // the fp16 copy of V (contiguous [B_v, T_k, HQ, D]) and its scale
+        uint32_t* amax = static_cast<uint32_t*>(ws);
+        float* vscale = reinterpret_cast<float*>(static_cast<char*>(ws) + 4);
+        __half* V16 = reinterpret_cast<__half*>(static_cast<char*>(ws) + 256 + sbytes);
+        const int64_t chunks = B_v * T_k * HQ * (D / 8);
+        int grid = num_sms() * 8;
+        if ((int64_t)grid * 256 > chunks) grid = (int)((chunks + 255) / 256);
+        if (cudaMemsetAsync(amax, 0, sizeof(uint32_t), stream) != cudaSuccess)
+            return fail(DSA_ERR_CUDA, "attn_tc: cudaMemsetAsync failed");
+        const __nv_bfloat16* Vb = static_cast<const __nv_bfloat16*>(V);
+        v_absmax_kernel<<<grid, 256, 0, stream>>>(Vb, T_k, (int)HQ, (int)D, L.V[0], L.V[1], L.V[2], chunks, amax);
+        int rc = check_launch("v_absmax_kernel");
+        if (rc) return rc;
+        v_to_f16_kernel<<<grid, 256, 0, stream>>>(Vb, T_k, (int)HQ, (int)D, L.V[0], L.V[1], L.V[2], chunks,
+                                                  amax, V16, vscale);
+        if ((rc = check_launch("v_to_f16_kernel"))) return rc;
+        p.vscale = vscale;
+        Vsrc = V16;
+        vst[2] = D;
+        vst[1] = HQ * D;
+        vst[0] = p.vshared ? 0 : T_k * HQ * D;
+    }
     {
-        const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)HQ, (cuuint64_t)T_k, (cuuint64_t)B};
-        const cuuint64_t str[3] = {(cuuint64_t)D * 2, (cuuint64_t)(HQ * D * 2),
-                                   (cuuint64_t)(T_k * HQ * D * 2)};
-        int rc = encode_map(&tmk, K, 4, dims, str, box, "attn_tc: K", dt);
+        // one map per tensor; a shared batch is a batch dimension of 1
+        const int64_t* st[2] = {L.K, vst};
+        const void* base[2] = {K, Vsrc};
+        const int shared[2] = {p.kshared, p.vshared};
+        const CUtensorMapDataType dts[2] = {dt, pv16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : dt};
+        CUtensorMap* m[2] = {&tmk, &tmv};
+        for (int x = 0; x < 2; ++x) {
+            const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)HQ, (cuuint64_t)T_k,
+                                        (cuuint64_t)(shared[x] ? 1 : B)};
+            const cuuint64_t str[3] = {(cuuint64_t)st[x][2] * 2, (cuuint64_t)st[x][1] * 2,
+                                       (cuuint64_t)(B > 1 && !shared[x] ? st[x][0] : st[x][1] * T_k) * 2};
+            int rc = encode_map(m[x], base[x], 4, dims, str, box, x ? "attn_tc: V" : "attn_tc: K", dts[x]);
+            if (rc) return rc;
+        }
+    }
+    if (skip && two) {
+        uint32_t* summ = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + 256);
+        block_summary_kernel<<<dim3((unsigned)p.n_qt, (unsigned)B), 256, 0, stream>>>(bits, words, T_q, p.n_qt,
+                                                                                   p.nkb, p.sw, summ);
+        const int rc = check_launch("block_summary_kernel");
         if (rc) return rc;
-        rc = encode_map(&tmv, V, 4, dims, str, box, "attn_tc: V", dt);
-        if (rc) return rc;
+        p.summ = summ;
     }
     auto kern = two ? kern2 : kern1;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)

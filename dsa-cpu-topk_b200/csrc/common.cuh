@@ -22,6 +22,26 @@ int check_launch(const char* what);
 int num_sms();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The caller's layout, or the contiguous one when it passed none.
+inline dsa_layout layout_or_contiguous(const dsa_layout* l, int64_t T_q, int64_t T_k, int64_t HI,
+                                       int64_t DI, int64_t HQ, int64_t DQ, int64_t DV) {
+    if (l) return *l;
+    dsa_layout c;
+    c.q[2] = DI; c.q[1] = HI * DI; c.q[0] = T_q * HI * DI;
+    c.k[1] = DI; c.k[0] = T_k * DI;
+    c.w[1] = HI; c.w[0] = T_q * HI;
+    c.Q[2] = DQ; c.Q[1] = HQ * DQ; c.Q[0] = T_q * HQ * DQ;
+    c.K[2] = DQ; c.K[1] = HQ * DQ; c.K[0] = T_k * HQ * DQ;
+    c.V[2] = DV; c.V[1] = HQ * DV; c.V[0] = T_k * HQ * DV;
+    c.row_bstep = 0;
+    return c;
+}
+// A byte stride a TMA tensor map accepts: a positive multiple of 16 below 2^40.
+inline bool tma_stride_ok(int64_t elems, int64_t elt) {
+    const int64_t b = elems * elt;
+    return b > 0 && (b & 15) == 0 && b < (int64_t(1) << 40);
+}
 inline size_t dtype_size(int dt) { return dt == DSA_F32 ? 4 : dt == DSA_FP8_E4M3 ? 1 : 2; }
 // dtypes of the indexer inputs (q, k); the attention inputs exclude FP8
 inline bool dtype_ok(int dt) {
@@ -73,13 +93,33 @@ __device__ __forceinline__ void unpack16<__half>(const uint4& v, float* out) {
     }
 }
 
-// Order-preserving map float -> uint32 (larger float -> larger key).
-// -0.0 is folded onto +0.0 so that key equality matches float ==.
+// Order-preserving map float -> uint32 (larger float -> larger key), with
+// the value order of torch.topk: -0.0 is folded onto +0.0 (key equality is
+// float ==), and every NaN, whatever its sign and payload, maps to the one
+// largest key KEY_NAN (torch.topk ranks NaN above +inf).  A NaN counts
+// towards the k largest but is never kept: the selection rule is
+// score >= threshold, which is false for NaN (see kept_key).
+constexpr uint32_t KEY_NAN = 0xffffffffu;
 __device__ __forceinline__ uint32_t f2key(float x) {
     // negative: ~b, positive: b | sign; then -0 (key 0x7fffffff) -> +0's key
     const uint32_t b = __float_as_uint(x);
     const uint32_t k = b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+    const uint32_t k0 = k == 0x7fffffffu ? 0x80000000u : k;
+    return (b & 0x7fffffffu) > 0x7f800000u ? KEY_NAN : k0;
+}
+// f2key without the NaN canonicalisation (NaNs keep distinct keys at both
+// ends: -NaN below -inf, +NaN above +inf).  Equal to f2key on every non-NaN
+// value; hot sweeps use it where a row without keys in the edge bins (which
+// hold every NaN) is then known to hold no NaN.
+__device__ __forceinline__ uint32_t f2key_raw(float x) {
+    const uint32_t b = __float_as_uint(x);
+    const uint32_t k = b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
     return k == 0x7fffffffu ? 0x80000000u : k;
+}
+// Whether a score of key `key` is kept under threshold key `thr_key`
+// (score >= thr as floats: NaN scores are never kept, a NaN threshold keeps nothing).
+__device__ __forceinline__ bool kept_key(uint32_t key, uint32_t thr_key) {
+    return key >= thr_key && key != KEY_NAN;
 }
 __device__ __forceinline__ float key2f(uint32_t k) {
     uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;

@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(32 * FS_ROWS) fused_small_kernel(FusedArgs<T> 
     // ---- 3. k-th largest (k_eff = min(k, T_k) counts the masked -inf entries)
     uint32_t thr_key;
     if (a.k > valid) {
-        thr_key = 0u;  // threshold -inf: every causal key is kept (key 0 < any real key)
+        thr_key = 0u;  // threshold -inf: every causal key but NaN is kept (key 0 < any real key)
     } else {
         uint32_t prefix = 0, pmask = 0, krem = (uint32_t)a.k;
 #pragma unroll 1
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(32 * FS_ROWS) fused_small_kernel(FusedArgs<T> 
     const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
     for (int i = 0; i < FS_NI; ++i) {
-        const bool p = lane + 32 * i < valid && key[i] >= thr_key;
+        const bool p = lane + 32 * i < valid && kept_key(key[i], thr_key);
         const uint32_t m = __ballot_sync(0xffffffffu, p);
         if (p) list[n + __popc(m & lt_mask)] = lane + 32 * i;
         n += __popc(m);

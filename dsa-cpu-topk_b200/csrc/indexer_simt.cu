@@ -25,13 +25,19 @@ namespace {
 
 constexpr int BT = 64, BS = 64, DC = 32;
 
+// element strides of q (batch, row, head), k (batch, row), w (batch, row) and
+// the per-batch step of the first query row
+struct SimtLayout {
+    int64_t qb, qr, qh, kb, kr, wb, wr, row_bstep;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__ q,
                                                           const T* __restrict__ k,
                                                           const float* __restrict__ w,
                                                           float* __restrict__ scores, int64_t T_q,
                                                           int64_t T_k, int64_t q_row0, int HI,
-                                                          int DI, int fill_upper) {
+                                                          int DI, int fill_upper, SimtLayout ly) {
     // [row][dim] with a 4-float pad: the float4 reads of 16 consecutive rows
     // (stride 36 words) fall in distinct bank quads.
     __shared__ __align__(16) float qs[BT][DC + 4];
@@ -42,6 +48,7 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
     const int64_t tq0 = (int64_t)blockIdx.y * BT;  // first query row (relative)
     const int64_t s0 = (int64_t)blockIdx.x * BS;
     const int64_t tq_end = tq0 + BT < T_q ? tq0 + BT : T_q;
+    q_row0 += b * ly.row_bstep;
     const int64_t t_max = q_row0 + tq_end - 1;
     float* srow0 = scores + (b * T_q) * T_k;
     const float NEG = -INFINITY;
@@ -62,8 +69,8 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) acc[i][jj] = 0.f;
 
-    const T* qb = q + (b * T_q) * (int64_t)HI * DI;
-    const T* kb = k + (b * T_k) * (int64_t)DI;
+    const T* qb = q + b * ly.qb;
+    const T* kb = k + b * ly.kb;
     for (int j = 0; j < HI; ++j) {
         float dot[4][4];
 #pragma unroll
@@ -78,8 +85,8 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
                 const int rr = e / DC, d = e % DC;
                 const int64_t tq = tq0 + rr, s = s0 + rr;
                 float qv = 0.f, kv = 0.f;
-                if (tq < T_q && dc + d < DI) qv = Elem<T>::to_f(qb[(tq * HI + j) * DI + dc + d]);
-                if (s < T_k && dc + d < DI) kv = Elem<T>::to_f(kb[s * DI + dc + d]);
+                if (tq < T_q && dc + d < DI) qv = Elem<T>::to_f(qb[tq * ly.qr + j * ly.qh + dc + d]);
+                if (s < T_k && dc + d < DI) kv = Elem<T>::to_f(kb[s * ly.kr + dc + d]);
                 qs[rr][d] = qv;
                 ks[rr][d] = kv;
             }
@@ -110,7 +117,7 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int64_t tq = tq0 + ty + 16 * i;
-            const float wv = tq < T_q ? w[(b * T_q + tq) * HI + j] : 0.f;
+            const float wv = tq < T_q ? w[b * ly.wb + tq * ly.wr + j] : 0.f;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(wv, fmaxf(dot[i][jj], 0.f), acc[i][jj]);
         }
@@ -140,7 +147,7 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
                                                                 float* __restrict__ scores,
                                                                 int64_t T_q, int64_t T_k,
                                                                 int64_t q_row0, int HI, int DI,
-                                                                int fill_upper) {
+                                                                int fill_upper, SimtLayout ly) {
     extern __shared__ __align__(16) float sm[];
     // row strides in floats: q rows are read as broadcasts, key rows by 16
     // lanes at once (stride DI+1 spreads them over distinct banks)
@@ -154,6 +161,7 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
     const int64_t tq0 = (int64_t)blockIdx.y * BT;
     const int64_t s0 = (int64_t)blockIdx.x * BS;
     const int64_t tq_end = tq0 + BT < T_q ? tq0 + BT : T_q;
+    q_row0 += b * ly.row_bstep;
     const int64_t t_max = q_row0 + tq_end - 1;
     float* srow0 = scores + (b * T_q) * T_k;
     const float NEG = -INFINITY;
@@ -167,15 +175,16 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
         return;
     }
     const int HD = HI * DI;
-    const T* qb = q + (b * T_q + tq0) * (int64_t)HD;
-    const T* kb = k + (b * T_k + s0) * (int64_t)DI;
+    const T* qb = q + b * ly.qb + tq0 * ly.qr;
+    const T* kb = k + b * ly.kb + s0 * ly.kr;
     for (int e = tid; e < BT * HD; e += 256) {
         const int r = e / HD, c = e - r * HD;
-        qs[r * QS + c] = tq0 + r < T_q ? Elem<T>::to_f(qb[e]) : 0.f;
+        const int hh = c / DI, d = c - hh * DI;
+        qs[r * QS + c] = tq0 + r < T_q ? Elem<T>::to_f(qb[r * ly.qr + hh * ly.qh + d]) : 0.f;
     }
     for (int e = tid; e < BS * DI; e += 256) {
         const int r = e / DI, c = e - r * DI;
-        ks[r * KS + c] = s0 + r < T_k ? Elem<T>::to_f(kb[e]) : 0.f;
+        ks[r * KS + c] = s0 + r < T_k ? Elem<T>::to_f(kb[r * ly.kr + c]) : 0.f;
     }
     __syncthreads();
 
@@ -227,7 +236,7 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int64_t tq = tq0 + ty + 16 * i;
-            const float wv = tq < T_q ? w[(b * T_q + tq) * HI + j] : 0.f;
+            const float wv = tq < T_q ? w[b * ly.wb + tq * ly.wr + j] : 0.f;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(wv, fmaxf(dot[i][jj], 0.f), acc[i][jj]);
         }
@@ -249,7 +258,7 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
 template <typename T>
 int launch(const void* q, const void* k, const float* w, float* scores, int64_t B, int64_t T_q,
            int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI, int fill_upper,
-           cudaStream_t stream) {
+           const SimtLayout& ly, cudaStream_t stream) {
     const int64_t gx = (T_k + BS - 1) / BS, gy = (T_q + BT - 1) / BT;
     if (gx > INT32_MAX || gy > 65535 || B > 65535)
         return fail(DSA_ERR_INVALID, "indexer: grid too large (T_q/64 and B must be <= 65535)");
@@ -261,11 +270,11 @@ int launch(const void* q, const void* k, const float* w, float* scores, int64_t 
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return fail(DSA_ERR_CUDA, "indexer: cannot set dynamic shared memory size");
         kern<<<grid, 256, smem, stream>>>((const T*)q, (const T*)k, w, scores, T_q, T_k, q_row0, (int)HI,
-                                          (int)DI, fill_upper);
+                                          (int)DI, fill_upper, ly);
         return check_launch("indexer_simt_small_kernel");
     }
     indexer_simt_kernel<T><<<grid, 256, 0, stream>>>((const T*)q, (const T*)k, w, scores, T_q, T_k,
-                                                     q_row0, (int)HI, (int)DI, fill_upper);
+                                                     q_row0, (int)HI, (int)DI, fill_upper, ly);
     return check_launch("indexer_simt_kernel");
 }
 
@@ -273,18 +282,19 @@ int launch(const void* q, const void* k, const float* w, float* scores, int64_t 
 
 int indexer_scores_simt(const void* q, const void* k, const float* w, float* scores, int64_t B,
                         int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                        int dtype, int fill_upper, cudaStream_t stream) {
+                        int dtype, int fill_upper, const dsa_layout& L, cudaStream_t stream) {
+    const SimtLayout ly{L.q[0], L.q[1], L.q[2], L.k[0], L.k[1], L.w[0], L.w[1], L.row_bstep};
     switch (dtype) {
         case DSA_F32:
-            return launch<float>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, stream);
+            return launch<float>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, ly, stream);
         case DSA_BF16:
-            return launch<__nv_bfloat16>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper,
+            return launch<__nv_bfloat16>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, ly,
                                          stream);
         case DSA_FP8_E4M3:
-            return launch<__nv_fp8_e4m3>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper,
+            return launch<__nv_fp8_e4m3>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, ly,
                                          stream);
         default:
-            return launch<__half>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, stream);
+            return launch<__half>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, ly, stream);
     }
 }
 

@@ -55,7 +55,11 @@ struct TcParams {
     float* scores;
     const float* w;
     int64_t T_q, T_k, q_row0;
+    int64_t row_bstep;          // batch b's rows start at q_row0 + b*row_bstep
+    int64_t wb, wr;             // element strides of w (batch, row)
     int HI, DI, B;
+    int flat;                   // tile prefix over (batch, query block) pairs (row blocks differ per batch)
+    int kshared;                // k has batch stride 0: every batch reads batch 0's keys
     int n_tblk, nsb, tiles_per_batch, total_tiles;
     int nA, nB;
     uint32_t a_bytes, b_bytes;
@@ -67,20 +71,31 @@ struct TcParams {
     unsigned long long timeout_ns;
 };
 
-// tile index -> (batch, query block, key block) through the per-batch prefix
-// of key blocks per query block
+// tile index -> (batch, query block, key block) through the prefix of key
+// blocks per query block: per batch when every batch has the same rows,
+// else over all (batch, query block) pairs
 __device__ __forceinline__ void decode_tile(int lin, const int* pref, const TcParams& p, int& b,
                                             int& i, int& j) {
-    b = lin / p.tiles_per_batch;
-    const int r = lin - b * p.tiles_per_batch;
-    int lo = 0, hi = p.n_tblk - 1;
+    int r = lin, n = p.n_tblk;
+    if (p.flat) {
+        n = p.B * p.n_tblk;
+    } else {
+        b = lin / p.tiles_per_batch;
+        r = lin - b * p.tiles_per_batch;
+    }
+    int lo = 0, hi = n - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (pref[mid] <= r) lo = mid;
         else hi = mid - 1;
     }
-    i = lo;
     j = r - pref[lo];
+    if (p.flat) {
+        b = lo / p.n_tblk;
+        i = lo - b * p.n_tblk;
+    } else {
+        i = lo;
+    }
 }
 
 template <bool FP8>
@@ -109,16 +124,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (threadIdx.x == 0) {
         int acc = 0;
-        for (int i = 0; i < p.n_tblk; ++i) {
-            pref[i] = acc;
+        const int nb = p.flat ? p.B : 1;
+        for (int x = 0; x < nb * p.n_tblk; ++x) {
+            const int bb = x / p.n_tblk, i = x - bb * p.n_tblk;
+            pref[x] = acc;
             int64_t tq_end = (int64_t)(i + 1) * BM;
             if (tq_end > p.T_q) tq_end = p.T_q;
-            const int64_t t_max = p.q_row0 + tq_end - 1;
+            const int64_t t_max = p.q_row0 + bb * p.row_bstep + tq_end - 1;
             int64_t c = t_max / BN + 1;
             if (c > p.nsb) c = p.nsb;
             acc += (int)c;
         }
-        pref[p.n_tblk] = acc;
+        pref[nb * p.n_tblk] = acc;
     }
     if (threadIdx.x == 32) {
         s_abort = 0;
@@ -161,7 +178,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!p.stall) mbar_expect_tx(&fullB[bs], p.b_bytes);
                 for (int c = 0; c < nch && !p.stall; ++c)
                     tma_load_3d(sB + (size_t)bs * p.b_bytes + (size_t)c * BN * 128, &tmk, &fullB[bs],
-                                c * kch, j * BN, b);
+                                c * kch, j * BN, p.kshared ? 0 : b);
                 if (++bs == p.nB) { bs = 0; bph ^= 1; }
                 for (int h = 0; h < p.HI; ++h) {
                     if (!(ok = mbar_wait(&emptyA[as], aph ^ 1, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
@@ -227,7 +244,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             decode_tile(lin, pref, p, b, i, j);
             const int64_t tq = (int64_t)i * BM + row;
             const bool row_ok = tq < p.T_q;
-            const float* wrow = p.w + ((int64_t)b * p.T_q + (row_ok ? tq : 0)) * p.HI;
+            const float* wrow = p.w + (int64_t)b * p.wb + (row_ok ? tq : 0) * p.wr;
             float acc[128];
 #pragma unroll
             for (int c = 0; c < 128; ++c) acc[c] = 0.f;
@@ -266,7 +283,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (++tb == 2) { tb = 0; tph ^= 1; }
                 }
             }
-            const int64_t t = p.q_row0 + tq;
+            const int64_t t = p.q_row0 + b * p.row_bstep + tq;
             const int64_t s0 = (int64_t)j * BN + half * 128;
             const float NEG = -INFINITY;
             if (p.tma_store) {
@@ -345,9 +362,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // -inf for every s > t (the full-matrix contract of the score output)
-__global__ void fill_upper_kernel(float* scores, int64_t T_q, int64_t T_k, int64_t q_row0) {
+__global__ void fill_upper_kernel(float* scores, int64_t T_q, int64_t T_k, int64_t q_row0,
+                                  int64_t row_bstep) {
     const int64_t row = blockIdx.x;  // b * T_q + tq
-    const int64_t t = q_row0 + row % T_q;
+    const int64_t t = q_row0 + (row / T_q) * row_bstep + row % T_q;
     float* out = scores + row * T_k;
     for (int64_t s = t + 1 + threadIdx.x; s < T_k; s += blockDim.x) out[s] = -INFINITY;
 }
@@ -383,9 +401,19 @@ static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64
 
 int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                      int fill_upper, int dtype, cudaStream_t stream) {
+                      int fill_upper, int dtype, const dsa_layout& L, cudaStream_t stream) {
     TcParams p;
     p.elt = dtype == DSA_FP8_E4M3 ? 1 : 2;
+    // tensor-map strides: positive multiples of 16 bytes (a batch stride of 0
+    // on k is read as one shared batch)
+    if (!tma_stride_ok(L.q[2], p.elt) || !tma_stride_ok(L.q[1], p.elt) ||
+        (B > 1 && !tma_stride_ok(L.q[0], p.elt)) || !tma_stride_ok(L.k[1], p.elt) ||
+        (B > 1 && L.k[0] != 0 && !tma_stride_ok(L.k[0], p.elt)))
+        return -100;
+    p.kshared = (B > 1 && L.k[0] == 0) ? 1 : 0;
+    p.row_bstep = L.row_bstep;
+    p.wb = L.w[0];
+    p.wr = L.w[1];
     const bool fp8 = p.elt == 1;
     auto kern = fp8 ? indexer_tc_kernel<true> : indexer_tc_kernel<false>;
     p.scores = scores;
@@ -399,17 +427,26 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     p.n_tblk = (int)((T_q + BM - 1) / BM);
     p.nsb = (int)((T_k + BN - 1) / BN);
     if (p.n_tblk > MAX_TBLK) return -100;  // caller falls back to the CUDA-core kernel
-    int64_t per_batch = 0;
-    for (int i = 0; i < p.n_tblk; ++i) {
-        int64_t tq_end = (int64_t)(i + 1) * BM;
-        if (tq_end > T_q) tq_end = T_q;
-        int64_t c = (q_row0 + tq_end - 1) / BN + 1;
-        if (c > p.nsb) c = p.nsb;
-        per_batch += c;
+    // batches whose rows start at different positions need the prefix over
+    // every (batch, query block); the caller splits larger calls per batch
+    p.flat = L.row_bstep != 0 ? 1 : 0;
+    if (p.flat && B * p.n_tblk > MAX_TBLK) return -101;
+    int64_t total = 0, per_batch = 0;
+    for (int64_t bb = 0; bb < (p.flat ? B : 1); ++bb) {
+        per_batch = 0;
+        for (int i = 0; i < p.n_tblk; ++i) {
+            int64_t tq_end = (int64_t)(i + 1) * BM;
+            if (tq_end > T_q) tq_end = T_q;
+            int64_t c = (q_row0 + bb * L.row_bstep + tq_end - 1) / BN + 1;
+            if (c > p.nsb) c = p.nsb;
+            per_batch += c;
+        }
+        total += per_batch;
     }
-    if (per_batch * B > INT32_MAX) return -100;
+    if (!p.flat) total = per_batch * B;
+    if (total > INT32_MAX) return -100;
     p.tiles_per_batch = (int)per_batch;
-    p.total_tiles = (int)(per_batch * B);
+    p.total_tiles = (int)total;
     p.a_bytes = (uint32_t)(BM * DI * p.elt);
     p.b_bytes = (uint32_t)(BN * DI * p.elt);
     p.vec_store = (T_k % 4 == 0) ? 1 : 0;
@@ -450,7 +487,7 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     const size_t smem = fixed + stage + (size_t)p.nA * p.a_bytes + (size_t)p.nB * p.b_bytes;
 
     if (fill_upper) {
-        fill_upper_kernel<<<(unsigned)(B * T_q), 256, 0, stream>>>(scores, T_q, T_k, q_row0);
+        fill_upper_kernel<<<(unsigned)(B * T_q), 256, 0, stream>>>(scores, T_q, T_k, q_row0, L.row_bstep);
         int rc = check_launch("fill_upper_kernel");
         if (rc) return rc;
     }
@@ -460,15 +497,17 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     {
         const cuuint64_t dims[4] = {(cuuint64_t)DI, (cuuint64_t)HI, (cuuint64_t)T_q, (cuuint64_t)B};
         const cuuint64_t e = (cuuint64_t)p.elt;
-        const cuuint64_t str[3] = {(cuuint64_t)DI * e, (cuuint64_t)HI * DI * e, (cuuint64_t)T_q * HI * DI * e};
+        const cuuint64_t str[3] = {(cuuint64_t)L.q[2] * e, (cuuint64_t)L.q[1] * e,
+                                   (cuuint64_t)(B > 1 ? L.q[0] : L.q[1] * T_q) * e};
         const cuuint32_t box[4] = {(cuuint32_t)(ROWB / p.elt), 1, BM, 1};
         int rc = encode_map(&tmq, q, 4, dims, str, box, "q", p.elt);
         if (rc) return rc;
     }
     {
-        const cuuint64_t dims[3] = {(cuuint64_t)DI, (cuuint64_t)T_k, (cuuint64_t)B};
+        const cuuint64_t dims[3] = {(cuuint64_t)DI, (cuuint64_t)T_k, (cuuint64_t)(p.kshared ? 1 : B)};
         const cuuint64_t e = (cuuint64_t)p.elt;
-        const cuuint64_t str[2] = {(cuuint64_t)DI * e, (cuuint64_t)T_k * DI * e};
+        const cuuint64_t str[2] = {(cuuint64_t)L.k[1] * e,
+                                   (cuuint64_t)(B > 1 && !p.kshared ? L.k[0] : L.k[1] * T_k) * e};
         const cuuint32_t box[3] = {(cuuint32_t)(ROWB / p.elt), BN, 1};
         int rc = encode_map(&tmk, k, 3, dims, str, box, "k", p.elt);
         if (rc) return rc;

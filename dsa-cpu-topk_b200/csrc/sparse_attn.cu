@@ -41,6 +41,10 @@ struct AttnArgs {
     int64_t B, T_q, T_k, q_row0;
     int HQ, D;
     float scale_log2;  // logit scale * log2(e)
+    // element strides (batch, row, head) of Q, K, V; batch b's rows start at
+    // q_row0 + b*row_bstep.  O is contiguous [B, T_q, HQ, D].
+    int64_t Qs[3], Ks[3], Vs[3];
+    int64_t row_bstep;
 };
 
 constexpr float kNegInf = -INFINITY;
@@ -117,18 +121,21 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
 
     const int64_t row = blockIdx.x;
     const int64_t b = row / a.T_q;
-    const int64_t t = a.q_row0 + (row - b * a.T_q);
+    const int64_t tq = row - b * a.T_q;
+    const int64_t t = a.q_row0 + b * a.row_bstep + tq;
     const int64_t valid = t + 1 < a.T_k ? t + 1 : a.T_k;
     const int64_t rowlen = (int64_t)a.HQ * a.D;
     // lane g of head h owns chunks g, g+G, ..., g+(C-1)G of the head, so each
     // chunk-load instruction reads a contiguous span per head
-    const int64_t toff = (int64_t)(lt / G) * a.D + (lt % G) * VEC;
-    const T* Kb = a.K + b * a.T_k * rowlen + toff;
-    const T* Vb = a.V + b * a.T_k * rowlen + toff;
+    const int64_t hd = lt / G, lo = (lt % G) * VEC;
+    const int64_t toff = hd * a.D + lo;   // in O
+    const T* Kb = a.K + b * a.Ks[0] + hd * a.Ks[2] + lo;
+    const T* Vb = a.V + b * a.Vs[0] + hd * a.Vs[2] + lo;
+    const int64_t kr = a.Ks[1], vr = a.Vs[1];
 
     float2 q[NP], acc[NP];
     {
-        const T* qp = a.Q + row * rowlen + toff;
+        const T* qp = a.Q + b * a.Qs[0] + tq * a.Qs[1] + hd * a.Qs[2] + lo;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const uint4 v = active ? ldg16(qp + c * G * VEC) : make_uint4(0, 0, 0, 0);
@@ -181,17 +188,17 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
         }
 
         for (int base = 0; base < n; base += P * U) {
-            uint4 kr[U][C], vr[U][C];
+            uint4 kreg[U][C], vreg[U][C];
             bool ok[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int j = base + team + u * P;
                 ok[u] = active && j < n;
-                const int64_t off = (ok[u] ? (int64_t)keys_s[j] : 0) * rowlen;
+                const int64_t key = ok[u] ? (int64_t)keys_s[j] : 0;
 #pragma unroll
                 for (int c = 0; c < C; ++c) {
-                    kr[u][c] = ok[u] ? ldg16(Kb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
-                    vr[u][c] = ok[u] ? ldg16(Vb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                    kreg[u][c] = ok[u] ? ldg16(Kb + key * kr + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                    vreg[u][c] = ok[u] ? ldg16(Vb + key * vr + c * G * VEC) : make_uint4(0, 0, 0, 0);
                 }
             }
             float x[U];
@@ -202,7 +209,7 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
 #pragma unroll
                 for (int c = 0; c < C; ++c)
 #pragma unroll
-                    for (int i = 0; i < PP; ++i) d2 = ffma2(q[c * PP + i], Pairs<T>::get(kr[u][c], i), d2);
+                    for (int i = 0; i < PP; ++i) d2 = ffma2(q[c * PP + i], Pairs<T>::get(kreg[u][c], i), d2);
                 float d = d2.x + d2.y;
 #pragma unroll
                 for (int o = G / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
@@ -227,7 +234,7 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
                 for (int c = 0; c < C; ++c)
 #pragma unroll
                     for (int i = 0; i < PP; ++i)
-                        acc[c * PP + i] = ffma2(p2, Pairs<T>::get(vr[u][c], i), acc[c * PP + i]);
+                        acc[c * PP + i] = ffma2(p2, Pairs<T>::get(vreg[u][c], i), acc[c * PP + i]);
             }
         }
         __syncthreads();
@@ -300,16 +307,19 @@ __global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
     const int team = lane / L;
     const int lt = lane - team * L;
     const int64_t b = row / a.T_q;
-    const int64_t t = a.q_row0 + (row - b * a.T_q);
+    const int64_t tq = row - b * a.T_q;
+    const int64_t t = a.q_row0 + b * a.row_bstep + tq;
     const int64_t valid = t + 1 < a.T_k ? t + 1 : a.T_k;
     const int64_t rowlen = (int64_t)a.HQ * a.D;
-    const int64_t toff = (int64_t)(lt / G) * a.D + (lt % G) * VEC;
-    const T* Kb = a.K + b * a.T_k * rowlen + toff;
-    const T* Vb = a.V + b * a.T_k * rowlen + toff;
+    const int64_t hd = lt / G, lo = (lt % G) * VEC;
+    const int64_t toff = hd * a.D + lo;   // in O
+    const T* Kb = a.K + b * a.Ks[0] + hd * a.Ks[2] + lo;
+    const T* Vb = a.V + b * a.Vs[0] + hd * a.Vs[2] + lo;
+    const int64_t kr = a.Ks[1], vr = a.Vs[1];
 
     float2 q[NP], acc[NP];
     {
-        const T* qp = a.Q + row * rowlen + toff;
+        const T* qp = a.Q + b * a.Qs[0] + tq * a.Qs[1] + hd * a.Qs[2] + lo;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const uint4 v = ldg16(qp + c * G * VEC);
@@ -349,18 +359,18 @@ __global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
             if (lane < n) mykey = (int)c0 + (int)__fns(bal, 0, lane + 1);
         }
         for (int base = 0; base < n; base += P * U) {
-            uint4 kr[U][C], vr[U][C];
+            uint4 kreg[U][C], vreg[U][C];
             bool ok[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int j = base + team + u * P;
                 ok[u] = j < n;
                 const int s = __shfl_sync(0xffffffffu, mykey, j & 31);
-                const int64_t off = (int64_t)(ok[u] ? s : 0) * rowlen;
+                const int64_t key = ok[u] ? s : 0;
 #pragma unroll
                 for (int c = 0; c < C; ++c) {
-                    kr[u][c] = ok[u] ? ldg16(Kb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
-                    vr[u][c] = ok[u] ? ldg16(Vb + off + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                    kreg[u][c] = ok[u] ? ldg16(Kb + key * kr + c * G * VEC) : make_uint4(0, 0, 0, 0);
+                    vreg[u][c] = ok[u] ? ldg16(Vb + key * vr + c * G * VEC) : make_uint4(0, 0, 0, 0);
                 }
             }
             float x[U];
@@ -371,7 +381,7 @@ __global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
 #pragma unroll
                 for (int c = 0; c < C; ++c)
 #pragma unroll
-                    for (int i = 0; i < PP; ++i) d2 = ffma2(q[c * PP + i], Pairs<T>::get(kr[u][c], i), d2);
+                    for (int i = 0; i < PP; ++i) d2 = ffma2(q[c * PP + i], Pairs<T>::get(kreg[u][c], i), d2);
                 float d = d2.x + d2.y;
 #pragma unroll
                 for (int o = G / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
@@ -396,7 +406,7 @@ __global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
                 for (int c = 0; c < C; ++c)
 #pragma unroll
                     for (int i = 0; i < PP; ++i)
-                        acc[c * PP + i] = ffma2(p2, Pairs<T>::get(vr[u][c], i), acc[c * PP + i]);
+                        acc[c * PP + i] = ffma2(p2, Pairs<T>::get(vreg[u][c], i), acc[c * PP + i]);
             }
         }
     }
@@ -492,9 +502,17 @@ int launch_t(AttnArgs<T> a, cudaStream_t stream) {
 int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const float* scores,
                 const float* thr, const void* Q, const void* K, const void* V, float* O, int64_t B,
                 int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t DQ, int64_t DV,
-                float scale, int dtype, cudaStream_t stream) {
+                float scale, int dtype, const dsa_layout& L, cudaStream_t stream) {
     if (B < 0 || T_q < 0 || T_k < 1 || q_row0 < 0 || HQ < 1 || DQ < 1 || DV < 1)
         return fail(DSA_ERR_INVALID, "sparse_attn: bad sizes");
+    {
+        // every gathered 16-byte chunk must stay aligned
+        const int64_t e = (int64_t)dtype_size(dtype);
+        for (const int64_t* st : {L.Q, L.K, L.V})
+            for (int i = 0; i < 3; ++i)
+                if ((st[i] * e) & 15)
+                    return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: Q/K/V strides must be multiples of 16 bytes");
+    }
     if (!dtype_ok(dtype)) return fail(DSA_ERR_INVALID, "sparse_attn: unknown dtype");
     if (dtype == DSA_FP8_E4M3)
         return fail(DSA_ERR_UNSUPPORTED, "sparse_attn: FP8 is supported for the indexer inputs only");
@@ -505,7 +523,8 @@ int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const f
         return fail(DSA_ERR_INVALID, "sparse_attn: Q/K/V/O must be 16-byte aligned");
     if (idx) {
         if (!cnt || idx_cap < 1) return fail(DSA_ERR_INVALID, "sparse_attn: idx needs cnt and idx_cap >= 1");
-        const int64_t longest = (q_row0 + T_q) < T_k ? (q_row0 + T_q) : T_k;
+        const int64_t last = q_row0 + (B > 0 ? B - 1 : 0) * (L.row_bstep > 0 ? L.row_bstep : 0) + T_q;
+        const int64_t longest = last < T_k ? last : T_k;
         if (idx_cap < longest && (!scores || !thr))
             return fail(DSA_ERR_INVALID,
                         "sparse_attn: idx_cap < longest row, so scores and thr are needed for overflow rows");
@@ -516,7 +535,9 @@ int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const f
     const float scale_log2 = scale * 1.4426950408889634f;
 #define DSA_ATTN_ARGS(TT)                                                                         \
     AttnArgs<TT> a{idx, cnt, idx_cap, scores, thr, (const TT*)Q, (const TT*)K, (const TT*)V, O, B, \
-                   T_q, T_k, q_row0, (int)HQ, (int)DQ, scale_log2};
+                   T_q, T_k, q_row0, (int)HQ, (int)DQ, scale_log2,                               \
+                   {L.Q[0], L.Q[1], L.Q[2]}, {L.K[0], L.K[1], L.K[2]}, {L.V[0], L.V[1], L.V[2]},   \
+                   L.row_bstep};
     if (dtype == DSA_F32) {
         DSA_ATTN_ARGS(float)
         return launch_t<float>(a, stream);

@@ -1,22 +1,34 @@
-// Stage 2: per-row top-K threshold + kept-index list by shared-memory radix select.
+// Stage 2: per-row top-K threshold and kept set by radix select.
 //
 // Replaces the GPU `scores.topk(k)` threshold of dsa_attention.py:343-344
 // (which materialises k values and indices per row only to read one column)
 // and the AVX-512 CPU k-th-largest of topk_avx512.cpp:226-249.
 //
-// One CTA owns one row at a time (grid-stride over rows).  The row is read
-// from HBM once: its order-preserving 32-bit keys are cached in shared memory
-// (up to cache_elems of them; a longer row re-reads the rest from L2).  Four
-// 8-bit radix passes narrow the k-th largest key from the top: each pass
-// histograms the digit of the keys that still match the selected prefix
-// (4 histogram copies, one per warp group, spread same-bin atomics), and a
-// 256-thread scan of the histogram picks the digit whose bin holds the k-th
-// largest.  The kept list is then written in ascending position order by a
-// warp-segmented ballot compaction, so the output is deterministic.
+// Scores become order-preserving 32-bit keys (f2key: -0 folded onto +0, every
+// NaN one key above +inf, as torch.topk ranks it).  The k-th largest key is
+// found digit by digit from the top; the kernel depends on the row length:
+//   <= 512      topk_warp_kernel: one warp per row, the keys in registers,
+//               four radix passes over a per-warp histogram, no block barriers
+//   513..4096   topk_warp_l2_kernel: one warp per row re-reading the row from
+//               L2 on each of its 9+8+8+7-bit passes
+//   4K..32K     topk_cached_kernel: one CTA per row.  One HBM sweep builds an
+//               11-bit first-digit histogram; a block scan finds the bin d0 of
+//               the k-th largest; the keys of bin d0 become candidates (with
+//               their positions) and two radix passes (11 + 10 bits) over the
+//               candidates give the exact key.  Bitmap rows write every word
+//               from the first digit in the candidate sweep and OR in the kept
+//               candidates; list rows emit ascending positions by
+//               warp-segmented ballots.  Rows up to 8K with lists cache the keys
+//               in shared memory; the others re-read the row from L2.
+//   > 32K       topk_select_kernel: four 8-bit passes, each filtering the row
+// Rows with fewer causal entries than k keep every causal entry (threshold
+// -inf).  Output is deterministic: lists are in ascending position order.
 //
 // Selection rule (dsa_attention.py:41-46): keep every position with
-// score >= threshold (ties kept) and, for causal rows, s <= t.
+// score >= threshold (ties kept, NaN never kept) and, for causal rows, s <= t.
 #include <stdlib.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -40,7 +52,95 @@ struct TopkArgs {
     int cache_elems;
     int cand_max;
     int vec_ok;
+    int64_t row_bstep;  // causal rows of batch bq sit at q_row0 + bq*row_bstep + (row % rows_per_batch)
 };
+
+// Causal length of a row: positions s <= t of query t (all of the row when not causal).
+__device__ __forceinline__ int64_t row_valid(const TopkArgs& a, int64_t row) {
+    if (!a.causal) return a.row_len;
+    const int64_t bq = row / a.rows_per_batch;
+    const int64_t t = a.q_row0 + bq * a.row_bstep + (row - bq * a.rows_per_batch);
+    return t + 1 < a.row_len ? t + 1 : a.row_len;
+}
+
+// A row with fewer causal entries than k (valid < k): the k-th largest is one
+// of the masked -inf entries, so the threshold is -inf and every causal entry
+// is kept except NaNs (NaN >= -inf is false).  One warp writes the threshold,
+// the count, the ascending index list and the bitmap words (zero past valid).
+__device__ __forceinline__ void short_row_warp(const TopkArgs& a, int64_t row, const float* src,
+                                               int64_t valid) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (valid + 31) >> 5;
+    const int64_t words = a.bits ? a.words : 0;
+    const int64_t end = nw > words ? nw : words;
+    uint32_t n = 0;
+    for (int64_t wd = 0; wd < end; ++wd) {
+        const int64_t s = wd * 32 + lane;
+        const bool p = s < valid && !isnan(__ldg(src + s));
+        const uint32_t m = __ballot_sync(0xffffffffu, p);
+        if (a.idx) {
+            const uint32_t pos = n + __popc(m & ((1u << lane) - 1u));
+            if (p && pos < (uint32_t)a.idx_cap) a.idx[row * a.idx_cap + pos] = (int32_t)s;
+        }
+        if (wd < words && lane == 0) a.bits[row * a.words + wd] = m;
+        n += __popc(m);
+    }
+    if (lane == 0) {
+        a.thr[row] = __uint_as_float(0xff800000u);
+        if (a.cnt) a.cnt[row] = (int32_t)n;
+    }
+}
+
+// short_row_warp for a whole CTA: warp w takes a contiguous run of words, so
+// the row is read by every warp at once (four words in flight per lane).
+// wtot holds BLOCK/32 words of shared memory; ends with a barrier.
+template <int BLOCK>
+__device__ __forceinline__ void short_row_block(const TopkArgs& a, int64_t row, const float* src,
+                                                int64_t valid, uint32_t* wtot) {
+    constexpr int NW = BLOCK / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t nw = (valid + 31) >> 5;
+    const int64_t words = a.bits ? a.words : 0;
+    const int64_t end = nw > words ? nw : words;
+    const int64_t seg = (end + NW - 1) / NW;
+    const int64_t w0 = warp * seg, w1 = w0 + seg < end ? w0 + seg : end;
+    auto word = [&](int64_t wd) {
+        const int64_t s = wd * 32 + lane;
+        return __ballot_sync(0xffffffffu, s < valid && !isnan(__ldg(src + s)));
+    };
+    uint32_t n = 0;
+    for (int64_t wd = w0; wd < w1; wd += 4) {
+        uint32_t m[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) m[u] = wd + u < w1 ? word(wd + u) : 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (wd + u < words && lane == 0) a.bits[row * a.words + wd + u] = m[u];
+            n += __popc(m[u]);
+        }
+    }
+    if (lane == 0) wtot[warp] = n;
+    __syncthreads();
+    uint32_t base = 0, tot = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < NW; ++w2) {
+        base += w2 < warp ? wtot[w2] : 0u;
+        tot += wtot[w2];
+    }
+    if (a.idx) {
+        for (int64_t wd = w0; wd < w1 && wd < nw; ++wd) {
+            const uint32_t m = word(wd);
+            const uint32_t pos = base + __popc(m & ((1u << lane) - 1u));
+            if (((m >> lane) & 1u) && pos < (uint32_t)a.idx_cap) a.idx[row * a.idx_cap + pos] = (int32_t)(wd * 32 + lane);
+            base += __popc(m);
+        }
+    }
+    if (threadIdx.x == 0) {
+        a.thr[row] = __uint_as_float(0xff800000u);
+        if (a.cnt) a.cnt[row] = (int32_t)tot;
+    }
+    __syncthreads();
+}
 
 template <int BLOCK>
 __device__ __forceinline__ uint32_t key_at(const uint32_t* cache, int ncache, const float* src,
@@ -62,23 +162,10 @@ __global__ void __launch_bounds__(BLOCK) topk_select_kernel(TopkArgs a) {
 
     for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
         const float* src = a.scores + row * a.row_stride;
-        int64_t valid = a.row_len;
-        if (a.causal) {
-            const int64_t t = a.q_row0 + row % a.rows_per_batch;
-            valid = t + 1 < a.row_len ? t + 1 : a.row_len;
-        }
+        const int64_t valid = row_valid(a, row);
 
         if ((int64_t)a.k > valid) {
-            // Fewer causal entries than k: the k-th largest is one of the
-            // masked -inf entries, so every causal position is kept.
-            if (tid == 0) {
-                a.thr[row] = __uint_as_float(0xff800000u);
-                if (a.cnt) a.cnt[row] = (int32_t)valid;
-            }
-            if (a.idx) {
-                const int64_t n = valid < a.idx_cap ? valid : a.idx_cap;
-                for (int64_t i = tid; i < n; i += BLOCK) a.idx[row * a.idx_cap + i] = (int32_t)i;
-            }
+            short_row_block<BLOCK>(a, row, src, valid, warp_tot);
             continue;  // block-uniform branch; no shared memory touched
         }
 
@@ -166,7 +253,7 @@ __global__ void __launch_bounds__(BLOCK) topk_select_kernel(TopkArgs a) {
             const int64_t s1 = s0 + seg < valid ? s0 + seg : valid;
             uint32_t c = 0;
             for (int64_t i = s0 + lane; i - lane < s1; i += 32) {
-                const bool p = i < s1 && key_at<BLOCK>(cache, ncache, src, i) >= thr_key;
+                const bool p = i < s1 && kept_key(key_at<BLOCK>(cache, ncache, src, i), thr_key);
                 c += __popc(__ballot_sync(0xffffffffu, p));
             }
             if (lane == 0) warp_tot[warp] = c;
@@ -181,7 +268,7 @@ __global__ void __launch_bounds__(BLOCK) topk_select_kernel(TopkArgs a) {
             if (a.idx) {
                 int32_t* out = a.idx + row * a.idx_cap;
                 for (int64_t i = s0 + lane; i - lane < s1; i += 32) {
-                    const bool p = i < s1 && key_at<BLOCK>(cache, ncache, src, i) >= thr_key;
+                    const bool p = i < s1 && kept_key(key_at<BLOCK>(cache, ncache, src, i), thr_key);
                     const uint32_t m = __ballot_sync(0xffffffffu, p);
                     const uint32_t pos = base + __popc(m & ((1u << lane) - 1u));
                     if (p && pos < a.idx_cap) out[pos] = (int32_t)i;
@@ -312,12 +399,12 @@ __device__ __forceinline__ uint4 group_keys(const uint4* cache4, const float* sr
 }
 
 // Kept-set bitmap of one row: bit s % 32 of word s / 32 is set iff s < valid
-// and key(s) >= thr_key (every s < valid when `all`).  Each thread turns one
+// and kept_key(key(s), thr_key).  Each thread turns one
 // float4 group into a nibble and eight lanes OR theirs into a word; words is
 // a multiple of 4, so every warp runs the same number of iterations.
 template <int BLOCK, bool CACHED>
 __device__ __forceinline__ void emit_bits(const TopkArgs& a, int64_t row, const float* src,
-                                          const uint4* cache4, int valid, uint32_t thr_key, bool all) {
+                                          const uint4* cache4, int valid, uint32_t thr_key) {
     uint32_t* out = a.bits + row * a.words;
     const int ng = (int)a.words * 8;
     const int g4 = (valid + 3) >> 2;
@@ -325,15 +412,10 @@ __device__ __forceinline__ void emit_bits(const TopkArgs& a, int64_t row, const 
     for (int g = threadIdx.x; g < ng; g += BLOCK) {
         uint32_t nib = 0;
         if (g < g4) {
-            if (all) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) nib |= (uint32_t)(4 * g + j < valid) << j;
-            } else {
-                // keys past `valid` are 0, below every real key
-                const uint4 kk = group_keys<CACHED>(cache4, src, g, valid, a.vec_ok);
-                nib = (uint32_t)(kk.x >= thr_key) | (uint32_t)(kk.y >= thr_key) << 1 |
-                      (uint32_t)(kk.z >= thr_key) << 2 | (uint32_t)(kk.w >= thr_key) << 3;
-            }
+            // keys past `valid` are 0, below every real key
+            const uint4 kk = group_keys<CACHED>(cache4, src, g, valid, a.vec_ok);
+            nib = (uint32_t)kept_key(kk.x, thr_key) | (uint32_t)kept_key(kk.y, thr_key) << 1 |
+                  (uint32_t)kept_key(kk.z, thr_key) << 2 | (uint32_t)kept_key(kk.w, thr_key) << 3;
         }
         uint32_t w = nib << (4 * (lane & 7));
         w |= __shfl_xor_sync(0xffffffffu, w, 1);
@@ -341,6 +423,71 @@ __device__ __forceinline__ void emit_bits(const TopkArgs& a, int64_t row, const 
         w |= __shfl_xor_sync(0xffffffffu, w, 4);
         if ((lane & 7) == 0) out[g >> 3] = w;
     }
+}
+
+// One row exactly, for rows holding NaN: four 8-bit radix passes over the
+// canonical keys (every NaN one key above +inf), re-reading the row from L2
+// each pass, then the count, the ascending list and the bitmap words.  Uses
+// hist[0..255]; ends with a barrier.  Kept out of line so the hot kernel's
+// register allocation does not carry it.
+template <int BLOCK>
+__device__ __noinline__ void exact_row_slow(const float* src, int valid, int k, float* thr_out,
+                                            int32_t* cnt_out, int32_t* idx_out, int64_t idx_cap,
+                                            uint32_t* bits_out, int64_t words, uint32_t* hist,
+                                            uint32_t* wtot, uint32_t* res) {
+    constexpr int NW = BLOCK / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint32_t prefix = 0, pmask = 0, krem = (uint32_t)k;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = tid; i < 256; i += BLOCK) hist[i] = 0;
+        __syncthreads();
+        for (int i = tid; i < valid; i += BLOCK) {
+            const uint32_t key = f2key(__ldg(src + i));
+            if ((key & pmask) == prefix) atomicAdd(&hist[255 - ((key >> shift) & 255u)], 1u);
+        }
+        __syncthreads();
+        block_find_desc<BLOCK>(hist, 256, krem, wtot, res);
+        prefix |= res[0] << shift;
+        pmask |= 255u << shift;
+        krem = res[1];
+    }
+    const uint32_t thr_key = prefix;
+    // warp w owns the contiguous segment [w*seg, (w+1)*seg) of the row
+    const int seg = ((valid + NW - 1) / NW + 31) & ~31;
+    const int s0 = warp * seg, s1 = s0 + seg < valid ? s0 + seg : valid;
+    uint32_t c = 0;
+    for (int i = s0 + lane; i - lane < s1; i += 32)
+        c += __popc(__ballot_sync(0xffffffffu, i < s1 && kept_key(f2key(__ldg(src + i)), thr_key)));
+    if (lane == 0) wtot[warp] = c;
+    __syncthreads();
+    uint32_t base = 0, tot = 0;
+    for (int w2 = 0; w2 < NW; ++w2) {
+        base += w2 < warp ? wtot[w2] : 0u;
+        tot += wtot[w2];
+    }
+    if (tid == 0) {
+        *thr_out = key2f(thr_key);
+        if (cnt_out) *cnt_out = (int32_t)tot;
+    }
+    if (idx_out) {
+        for (int i = s0 + lane; i - lane < s1; i += 32) {
+            const bool p = i < s1 && kept_key(f2key(__ldg(src + i)), thr_key);
+            const uint32_t m = __ballot_sync(0xffffffffu, p);
+            const uint32_t pos = base + __popc(m & ((1u << lane) - 1u));
+            if (p && pos < idx_cap) idx_out[pos] = i;
+            base += __popc(m);
+        }
+    }
+    if (bits_out) {
+        for (int64_t wd = warp; wd < words; wd += NW) {
+            const int64_t s = wd * 32 + lane;
+            const bool p = s < valid && kept_key(f2key(__ldg(src + s)), thr_key);
+            const uint32_t m = __ballot_sync(0xffffffffu, p);
+            if (lane == 0) bits_out[wd] = m;
+        }
+    }
+    __syncthreads();
 }
 
 template <int BLOCK, bool CACHED>
@@ -362,26 +509,14 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
 
     for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
         const float* src = a.scores + row * a.row_stride;
-        int valid = (int)a.row_len;
-        if (a.causal) {
-            const int64_t t = a.q_row0 + row % a.rows_per_batch;
-            valid = t + 1 < a.row_len ? (int)(t + 1) : (int)a.row_len;
-        }
+        const int valid = (int)row_valid(a, row);
         if (a.k > valid) {
-            if (tid == 0) {
-                a.thr[row] = __uint_as_float(0xff800000u);
-                if (a.cnt) a.cnt[row] = valid;
-            }
-            if (a.idx) {
-                const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
-                for (int i = tid; i < n; i += BLOCK) a.idx[row * a.idx_cap + i] = i;
-            }
-            if (a.bits) emit_bits<BLOCK, CACHED>(a, row, src, dyn4, valid, 0u, true);
-            continue;
+            short_row_block<BLOCK>(a, row, src, valid, wtot);
+            continue;  // block-uniform branch
         }
         const int g4 = (valid + 3) >> 2;  // uint4 groups; padding keys are 0
 
-        // ---- sweep 1
+        // ---- sweep 1 (raw keys: equal to f2key on rows without NaN, see below)
         for (int i = tid; i < NB_TOP; i += BLOCK) hist[i] = 0;
         if (tid == 0) n_cand = 0;
         __syncthreads();
@@ -401,7 +536,8 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                 for (int u = 0; u < PIPE; ++u) {
                     const int g = g0 + u * BLOCK;
                     if (g < gfull) {
-                        const uint4 kk = make_uint4(f2key(v[u].x), f2key(v[u].y), f2key(v[u].z), f2key(v[u].w));
+                        const uint4 kk = make_uint4(f2key_raw(v[u].x), f2key_raw(v[u].y), f2key_raw(v[u].z),
+                                                    f2key_raw(v[u].w));
                         atomicAdd(&hist[(NB_TOP - 1) - (kk.x >> S0)], 1u);
                         atomicAdd(&hist[(NB_TOP - 1) - (kk.y >> S0)], 1u);
                         atomicAdd(&hist[(NB_TOP - 1) - (kk.z >> S0)], 1u);
@@ -414,7 +550,7 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                 uint32_t e[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    e[j] = 4 * gfull + j < valid ? f2key(__ldg(src + 4 * gfull + j)) : 0u;
+                    e[j] = 4 * gfull + j < valid ? f2key_raw(__ldg(src + 4 * gfull + j)) : 0u;
                     if (4 * gfull + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
                 }
                 if (CACHED) dyn4[gfull] = make_uint4(e[0], e[1], e[2], e[3]);
@@ -424,21 +560,33 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                 uint32_t e[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
+                    e[j] = 4 * g + j < valid ? f2key_raw(__ldg(src + 4 * g + j)) : 0u;
                     if (4 * g + j < valid) atomicAdd(&hist[(NB_TOP - 1) - (e[j] >> S0)], 1u);
                 }
                 if (CACHED) dyn4[g] = make_uint4(e[0], e[1], e[2], e[3]);
             }
         }
         __syncthreads();
-        block_find_desc<BLOCK>(hist, NB_TOP, (uint32_t)a.k, wtot, res);
-        const uint32_t d0 = res[0];
-        uint32_t krem = res[1];
-        const bool use_cand = hist[(NB_TOP - 1) - d0] <= (uint32_t)a.cand_max;
         // no key in bins 0-3 or 2044-2047 (NaNs, infinities and their
         // neighbours): float order is key order on this row
         const bool plain = (hist[0] | hist[1] | hist[2] | hist[3] | hist[NB_TOP - 4] | hist[NB_TOP - 3] |
                             hist[NB_TOP - 2] | hist[NB_TOP - 1]) == 0u;
+        if (!plain) {
+            // every NaN falls in those bins; a row that holds one takes the
+            // exact slow path with NaN-canonical keys (rare rows)
+            bool nan_here = false;
+            for (int i = tid; i < valid && !nan_here; i += BLOCK) nan_here = isnan(__ldg(src + i));
+            if (__syncthreads_or(nan_here)) {
+                exact_row_slow<BLOCK>(src, valid, a.k, a.thr + row, a.cnt ? a.cnt + row : nullptr,
+                                      a.idx ? a.idx + row * a.idx_cap : nullptr, a.idx_cap,
+                                      a.bits ? a.bits + row * a.words : nullptr, a.words, hist, wtot, res);
+                continue;   // block-uniform
+            }
+        }
+        block_find_desc<BLOCK>(hist, NB_TOP, (uint32_t)a.k, wtot, res);
+        const uint32_t d0 = res[0];
+        uint32_t krem = res[1];
+        const bool use_cand = hist[(NB_TOP - 1) - d0] <= (uint32_t)a.cand_max;
         __syncthreads();
 
         // warp w owns groups [w*gseg, min((w+1)*gseg, g4))
@@ -502,7 +650,7 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                         for (int j = 0; j < 4; ++j)
                             if (e[j] >= lo_f && e[j] < hi_f) {
                                 const uint32_t at = atomicAdd(&n_cand, 1u);
-                                cand_key[at] = f2key(e[j]);
+                                cand_key[at] = f2key_raw(e[j]);   // no NaN on this path
                                 cand_pos[at] = 4 * g + j;
                             }
                     }
@@ -565,7 +713,7 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
             // the words are written (the barriers above order them before the ORs)
             uint32_t kc = 0;
             for (int i = tid; i < nc; i += BLOCK)
-                if (cand_key[i] >= prefix) {
+                if (kept_key(cand_key[i], prefix)) {
                     atomicOr(out + (cand_pos[i] >> 5), 1u << (cand_pos[i] & 31));
                     ++kc;
                 }
@@ -637,7 +785,7 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                 krem = res[1];
             }
             for (int i = tid; i < nc; i += BLOCK)
-                if (cand_key[i] >= prefix) atomicAdd(&seg_cnt[(cand_pos[i] >> 2) / gseg], 1u);
+                if (kept_key(cand_key[i], prefix)) atomicAdd(&seg_cnt[(cand_pos[i] >> 2) / gseg], 1u);
             __syncthreads();
         } else {
 #pragma unroll 1
@@ -663,7 +811,8 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
             uint32_t c = 0;
             for (int g = gs0 + lane; g < gs1; g += 32) {
                 const uint4 kk = group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok);
-                c += (kk.x >= prefix) + (kk.y >= prefix) + (kk.z >= prefix) + (kk.w >= prefix);
+                c += kept_key(kk.x, prefix) + kept_key(kk.y, prefix) + kept_key(kk.z, prefix) +
+                     kept_key(kk.w, prefix);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
@@ -697,8 +846,8 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
             for (int gb = gs0; gb < gs1 && base < cap; gb += 32) {
                 const int g = gb + lane;
                 const uint4 kk = g < gs1 ? group_keys<CACHED>(dyn4, src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
-                const bool p0 = kk.x >= thr_key, p1 = kk.y >= thr_key, p2 = kk.z >= thr_key,
-                           p3 = kk.w >= thr_key;
+                const bool p0 = kept_key(kk.x, thr_key), p1 = kept_key(kk.y, thr_key),
+                           p2 = kept_key(kk.z, thr_key), p3 = kept_key(kk.w, thr_key);
                 const uint32_t n = p0 + p1 + p2 + p3;
                 uint32_t pre = n;
 #pragma unroll
@@ -717,7 +866,7 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                 base += __shfl_sync(0xffffffffu, pre, 31);
             }
         }
-        if (a.bits) emit_bits<BLOCK, CACHED>(a, row, src, dyn4, valid, thr_key, false);
+        if (a.bits) emit_bits<BLOCK, CACHED>(a, row, src, dyn4, valid, thr_key);
         __syncthreads();
     }
 }
@@ -763,20 +912,9 @@ __global__ void __launch_bounds__(256) topk_warp_kernel(TopkArgs a) {
 
     for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.n_rows; row += (int64_t)gridDim.x * 8) {
         const float* src = a.scores + row * a.row_stride;
-        int valid = (int)a.row_len;
-        if (a.causal) {
-            const int64_t t = a.q_row0 + row % a.rows_per_batch;
-            valid = t + 1 < a.row_len ? (int)(t + 1) : (int)a.row_len;
-        }
+        const int valid = (int)row_valid(a, row);
         if (a.k > valid) {
-            if (lane == 0) {
-                a.thr[row] = __uint_as_float(0xff800000u);
-                if (a.cnt) a.cnt[row] = valid;
-            }
-            if (a.idx) {
-                const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
-                for (int i = lane; i < n; i += 32) a.idx[row * a.idx_cap + i] = i;
-            }
+            short_row_warp(a, row, src, valid);
             continue;
         }
         // ---- load: group g = lane + 32j holds positions 4g..4g+3; padding keys are 0
@@ -857,7 +995,7 @@ __global__ void __launch_bounds__(256) topk_warp_kernel(TopkArgs a) {
             const int g = lane + 32 * j;
             bool pk[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) pk[e] = 4 * g + e < valid && key[j][e] >= thr_key;
+            for (int e = 0; e < 4; ++e) pk[e] = 4 * g + e < valid && kept_key(key[j][e], thr_key);
             const uint32_t m0 = __ballot_sync(0xffffffffu, pk[0]), m1 = __ballot_sync(0xffffffffu, pk[1]),
                            m2 = __ballot_sync(0xffffffffu, pk[2]), m3 = __ballot_sync(0xffffffffu, pk[3]);
             if (out) {
@@ -907,18 +1045,84 @@ int launch_warp(const TopkArgs& a, cudaStream_t stream) {
 // ===========================================================================
 constexpr int WL2_BINS = 512;
 
+// Keys of group g: canonical (f2key) or raw (f2key_raw, equal on rows without NaN)
+template <bool CANON>
 __device__ __forceinline__ uint4 row_keys4(const float* src, int g, int valid, int vec_ok) {
+    auto key = [](float x) { return CANON ? f2key(x) : f2key_raw(x); };
     if (vec_ok && 4 * g + 3 < valid) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(src) + g);
-        return make_uint4(f2key(v.x), f2key(v.y), f2key(v.z), f2key(v.w));
+        return make_uint4(key(v.x), key(v.y), key(v.z), key(v.w));
     }
     uint32_t e[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) e[j] = 4 * g + j < valid ? f2key(__ldg(src + 4 * g + j)) : 0u;
+    for (int j = 0; j < 4; ++j) e[j] = 4 * g + j < valid ? key(__ldg(src + 4 * g + j)) : 0u;
     return make_uint4(e[0], e[1], e[2], e[3]);
 }
 
-__global__ void __launch_bounds__(256) topk_warp_l2_kernel(TopkArgs a) {
+// One row exactly, by one warp, for rows holding NaN: four 8-bit radix passes
+// over the canonical keys (every NaN one key above +inf) re-reading the row,
+// then the count and the ascending list.  hist: the warp's >= 256 slots.
+// Kept out of line so the hot kernel's register allocation does not carry it.
+__device__ __noinline__ void warp_exact_row_slow(const float* src, int valid, int k, float* thr_out,
+                                                 int32_t* cnt_out, int32_t* idx_out, int64_t idx_cap,
+                                                 uint32_t* hist) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0, pmask = 0, krem = (uint32_t)k;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = lane; i < 256; i += 32) hist[i] = 0;
+        __syncwarp();
+        for (int i = lane; i < valid; i += 32) {
+            const uint32_t key = f2key(__ldg(src + i));
+            if ((key & pmask) == prefix) atomicAdd(&hist[255 - ((key >> shift) & 255u)], 1u);
+        }
+        __syncwarp();
+        // lane owns slots 8*lane .. 8*lane+7 (descending digits)
+        uint32_t local = 0;
+        for (int q = 0; q < 8; ++q) local += hist[lane * 8 + q];
+        uint32_t incl = local;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint32_t excl = incl - local;
+        const bool mine = excl < krem && krem <= incl;
+        uint32_t dig = 0, kr = 0;
+        if (mine) {
+            uint32_t c = excl;
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t h = hist[lane * 8 + q];
+                if (krem <= c + h) {
+                    dig = (uint32_t)(255 - (lane * 8 + q));
+                    kr = krem - c;
+                    break;
+                }
+                c += h;
+            }
+        }
+        const uint32_t who = __ballot_sync(0xffffffffu, mine);
+        const int srcl = who ? __ffs(who) - 1 : 0;
+        prefix |= __shfl_sync(0xffffffffu, dig, srcl) << shift;
+        pmask |= 255u << shift;
+        krem = __shfl_sync(0xffffffffu, kr, srcl);
+        __syncwarp();
+    }
+    uint32_t n = 0;
+    for (int i0 = 0; i0 < valid; i0 += 32) {
+        const int i = i0 + lane;
+        const bool p = i < valid && kept_key(f2key(__ldg(src + i)), prefix);
+        const uint32_t m = __ballot_sync(0xffffffffu, p);
+        const uint32_t pos = n + __popc(m & ((1u << lane) - 1u));
+        if (idx_out && p && pos < idx_cap) idx_out[pos] = i;
+        n += __popc(m);
+    }
+    if (lane == 0) {
+        *thr_out = key2f(prefix);
+        if (cnt_out) *cnt_out = (int32_t)n;
+    }
+}
+
+__global__ void __launch_bounds__(256, 5) topk_warp_l2_kernel(TopkArgs a) {
     extern __shared__ uint4 wl2_dyn[];  // 8 warps x WL2_BINS
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t* hist = reinterpret_cast<uint32_t*>(wl2_dyn) + warp * WL2_BINS;
@@ -926,24 +1130,14 @@ __global__ void __launch_bounds__(256) topk_warp_l2_kernel(TopkArgs a) {
 
     for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < a.n_rows; row += (int64_t)gridDim.x * 8) {
         const float* src = a.scores + row * a.row_stride;
-        int valid = (int)a.row_len;
-        if (a.causal) {
-            const int64_t t = a.q_row0 + row % a.rows_per_batch;
-            valid = t + 1 < a.row_len ? (int)(t + 1) : (int)a.row_len;
-        }
+        const int valid = (int)row_valid(a, row);
         if (a.k > valid) {
-            if (lane == 0) {
-                a.thr[row] = __uint_as_float(0xff800000u);
-                if (a.cnt) a.cnt[row] = valid;
-            }
-            if (a.idx) {
-                const int n = valid < a.idx_cap ? valid : (int)a.idx_cap;
-                for (int i = lane; i < n; i += 32) a.idx[row * a.idx_cap + i] = i;
-            }
+            short_row_warp(a, row, src, valid);
             continue;
         }
         const int g4 = (valid + 3) >> 2;
         uint32_t prefix = 0, pmask = 0, krem = (uint32_t)a.k, bin_n = 0;
+        bool slow = false;
 #pragma unroll 1
         for (int pass = 0; pass < 4; ++pass) {
             const int bits = pass == 0 ? 9 : pass == 3 ? 7 : 8;
@@ -953,25 +1147,37 @@ __global__ void __launch_bounds__(256) topk_warp_l2_kernel(TopkArgs a) {
 #pragma unroll
             for (int q = 0; q < WL2_BINS / 128; ++q) reinterpret_cast<uint4*>(hist)[lane + 32 * q] = make_uint4(0, 0, 0, 0);
             __syncwarp();
-            // slot = WL2_BINS - 1 - digit (descending digits)
-            for (int g0 = lane; g0 < g4; g0 += 32 * 4) {
-                uint4 kk[4];
+            // slot = WL2_BINS - 1 - digit (descending digits).  The first pass
+            // uses canonical keys (every NaN in digit 511, beside +inf), the
+            // later ones raw keys: they are equal on rows without NaN, and a
+            // row with anything in digit 511 takes the exact slow path.
+            auto accumulate = [&](auto canon_tag) {
+                constexpr bool CANON = decltype(canon_tag)::value;
+                for (int g0 = lane; g0 < g4; g0 += 32 * 4) {
+                    uint4 kk[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int g = g0 + 32 * u;
-                    kk[u] = g < g4 ? row_keys4(src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
+                    for (int u = 0; u < 4; ++u) {
+                        const int g = g0 + 32 * u;
+                        kk[u] = g < g4 ? row_keys4<CANON>(src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int g = g0 + 32 * u;
+                        const uint32_t e[4] = {kk[u].x, kk[u].y, kk[u].z, kk[u].w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (4 * g + j < valid && (e[j] & pmask) == prefix)
+                                atomicAdd(&hist[(WL2_BINS - 1) - ((e[j] >> shift) & (nb - 1))], 1u);
+                    }
                 }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int g = g0 + 32 * u;
-                    const uint32_t e[4] = {kk[u].x, kk[u].y, kk[u].z, kk[u].w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        if (4 * g + j < valid && (e[j] & pmask) == prefix)
-                            atomicAdd(&hist[(WL2_BINS - 1) - ((e[j] >> shift) & (nb - 1))], 1u);
-                }
-            }
+            };
+            if (pass == 0) accumulate(std::true_type{});
+            else accumulate(std::false_type{});
             __syncwarp();
+            if (pass == 0 && hist[0]) {   // +inf or NaN in the row (rare)
+                slow = true;
+                break;
+            }
             // warp scan: lane owns slots [SPL*lane, SPL*lane+SPL)
             constexpr int SPL = WL2_BINS / 32;
             uint32_t local = 0;
@@ -1012,6 +1218,11 @@ __global__ void __launch_bounds__(256) topk_warp_l2_kernel(TopkArgs a) {
             krem = kr;
             __syncwarp();
         }
+        if (slow) {
+            warp_exact_row_slow(src, valid, a.k, a.thr + row, a.cnt ? a.cnt + row : nullptr,
+                                a.idx ? a.idx + row * a.idx_cap : nullptr, a.idx_cap, hist);
+            continue;
+        }
         const uint32_t thr_key = prefix;
         // kept = keys above the k-th (k - krem of them) + keys equal to it (the final bin)
         const uint32_t total = (uint32_t)a.k - krem + bin_n;
@@ -1025,9 +1236,11 @@ __global__ void __launch_bounds__(256) topk_warp_l2_kernel(TopkArgs a) {
             uint32_t base = 0;
             for (int gb = 0; gb < g4 && base < cap; gb += 32) {
                 const int g = gb + lane;
-                const uint4 kk = g < g4 ? row_keys4(src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
-                const bool p0 = 4 * g < valid && kk.x >= thr_key, p1 = 4 * g + 1 < valid && kk.y >= thr_key,
-                           p2 = 4 * g + 2 < valid && kk.z >= thr_key, p3 = 4 * g + 3 < valid && kk.w >= thr_key;
+                const uint4 kk = g < g4 ? row_keys4<false>(src, g, valid, a.vec_ok) : make_uint4(0, 0, 0, 0);
+                const bool p0 = 4 * g < valid && kept_key(kk.x, thr_key),
+                           p1 = 4 * g + 1 < valid && kept_key(kk.y, thr_key),
+                           p2 = 4 * g + 2 < valid && kept_key(kk.z, thr_key),
+                           p3 = 4 * g + 3 < valid && kept_key(kk.w, thr_key);
                 const uint32_t m0 = __ballot_sync(0xffffffffu, p0), m1 = __ballot_sync(0xffffffffu, p1),
                                m2 = __ballot_sync(0xffffffffu, p2), m3 = __ballot_sync(0xffffffffu, p3);
                 uint32_t pos = base + __popc(m0 & lt_mask) + __popc(m1 & lt_mask) + __popc(m2 & lt_mask) +
@@ -1061,7 +1274,7 @@ int launch_warp_l2(const TopkArgs& a, cudaStream_t stream) {
 }  // namespace
 
 int kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B, int64_t T_q,
-                int64_t T_k, int64_t q_row0, int64_t words, cudaStream_t stream);
+                int64_t T_k, int64_t q_row0, int64_t words, int64_t row_bstep, cudaStream_t stream);
 int64_t bitmap_words(int64_t T_k);
 
 static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream);
@@ -1069,7 +1282,7 @@ static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
                 int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
                 int32_t* idx, int32_t* cnt, int64_t idx_cap, uint32_t* bits, int64_t words,
-                cudaStream_t stream) {
+                int64_t row_bstep, cudaStream_t stream) {
     if (n_rows < 0 || row_len < 1 || row_stride < row_len)
         return fail(DSA_ERR_INVALID, "topk_select: need n_rows >= 0, row_len >= 1, row_stride >= row_len");
     if (k < 1 || k > row_len)
@@ -1078,6 +1291,10 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     if (row_len > INT32_MAX || k > INT32_MAX) return fail(DSA_ERR_INVALID, "topk_select: row too long");
     if (causal && rows_per_batch < 1) return fail(DSA_ERR_INVALID, "topk_select: rows_per_batch < 1");
     if (q_row0 < 0) return fail(DSA_ERR_INVALID, "topk_select: q_row0 < 0");
+    if (causal && n_rows % rows_per_batch && row_bstep)
+        return fail(DSA_ERR_INVALID, "topk_select: row_bstep needs n_rows a multiple of rows_per_batch");
+    if (causal && q_row0 + (n_rows / rows_per_batch) * (row_bstep < 0 ? row_bstep : 0) < 0)
+        return fail(DSA_ERR_INVALID, "topk_select: a row block starts before position 0");
     if (!scores || !thr) return fail(DSA_ERR_INVALID, "topk_select: scores and thr_out are required");
     if (idx && idx_cap < 1) return fail(DSA_ERR_INVALID, "topk_select: idx_cap < 1 with idx_out");
     if (bits && (words < bitmap_words(row_len) || (words & 3) || row_stride != row_len))
@@ -1092,6 +1309,7 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     a.row_stride = row_stride;
     a.rows_per_batch = causal ? rows_per_batch : 1;
     a.q_row0 = q_row0;
+    a.row_bstep = causal ? row_bstep : 0;
     a.causal = causal ? 1 : 0;
     a.k = (int)k;
     a.thr = thr;
@@ -1104,7 +1322,9 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     // longest row any CTA will see
     int64_t longest = row_len;
     if (causal) {
-        const int64_t tmax = q_row0 + (n_rows < rows_per_batch ? n_rows : rows_per_batch) - 1;
+        const int64_t nbat = (n_rows + rows_per_batch - 1) / rows_per_batch;
+        const int64_t step = row_bstep > 0 ? row_bstep : 0;
+        const int64_t tmax = q_row0 + (nbat - 1) * step + (n_rows < rows_per_batch ? n_rows : rows_per_batch) - 1;
         longest = tmax + 1 < row_len ? tmax + 1 : row_len;
     }
     constexpr int64_t kCacheMax = 12288;  // 48 KB of keys per CTA
@@ -1118,7 +1338,7 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     // causal rows: key s kept only if s <= q_row0 + r % rows_per_batch;
     // otherwise a q_row0 past the row end makes every position causal
     return kept_bitmap(scores, thr, bits, n_rows / a.rows_per_batch, a.rows_per_batch, row_len,
-                       causal ? q_row0 : row_len, words, stream);
+                       causal ? q_row0 : row_len, words, a.row_bstep, stream);
 }
 
 static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream) {

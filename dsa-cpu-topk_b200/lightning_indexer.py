@@ -49,20 +49,24 @@ def indexer_scores_triton(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor,
 
 
 def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, q_row0: int = 0,
-                   fill_upper: bool = True) -> torch.Tensor:
-    """Scores of query rows q_row0..q_row0+T_q-1 against keys 0..T_k-1.
+                   row_bstep: int = 0, fill_upper: bool = True) -> torch.Tensor:
+    """Scores of query rows q_row0 + b*row_bstep + i (i < T_q) against keys 0..T_k-1.
 
-    q: [B,T_q,H,d], k: [B,T_k,d], w: [B,T_q,H] -> [B,T_q,T_k] fp32.
+    q: [B,T_q,H,d], k: [B,T_k,d] (or [1,T_k,d], shared), w: [B,T_q,H] -> [B,T_q,T_k]
+    fp32.  Strided views are read in place.
     """
     assert q.dim() == 4 and k.dim() == 3 and w.dim() == 3
     B, T_q, H, d = q.shape
-    assert k.shape[0] == B and k.shape[2] == d and w.shape == (B, T_q, H)
+    assert k.shape[0] in (B, 1) and k.shape[2] == d and w.shape == (B, T_q, H)
     if k.dtype != q.dtype:
         k = k.to(q.dtype)
-    q, k = _native.prep(q), _native.prep(k)
-    w = _native.prep(w.float())
+    if k.shape[0] != B:
+        k = k.expand(B, *k.shape[1:])
+    w = w if w.dtype == torch.float32 else w.float()
+    q, k, w = _native.prep_strided(q), _native.prep_strided(k), _native.prep_strided(w)
     scores = torch.empty((B, T_q, k.shape[1]), device=q.device, dtype=torch.float32)
-    _native.indexer_scores(q, k, w, scores, q_row0=q_row0, fill_upper=fill_upper)
+    _native.indexer_scores_ex(q, k, w, scores, q_row0=q_row0, row_bstep=row_bstep,
+                              fill_upper=fill_upper)
     return scores
 
 

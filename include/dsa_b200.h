@@ -11,7 +11,9 @@
  *
  * Conventions shared by every entry point
  *   - All pointers are device pointers on the current CUDA device, row-major
- *     and contiguous in the layouts given below, 16-byte aligned.
+ *     and contiguous in the layouts given below, 16-byte aligned.  The _ex
+ *     entry points take the input tensors with arbitrary element strides
+ *     (struct dsa_layout) instead.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
  *     Every call only enqueues work: nothing synchronises, nothing allocates.
  *     The caller owns every buffer, outputs and workspaces included.
@@ -64,6 +66,42 @@ typedef enum {
 /* DSA_FP8_E4M3 is accepted for the indexer inputs (q, k) only. */
 typedef enum { DSA_F32 = 0, DSA_BF16 = 1, DSA_F16 = 2, DSA_FP8_E4M3 = 3 } dsa_dtype;
 
+/*
+ * Strided inputs and row blocks (the _ex entry points).
+ *
+ * Element strides of each input tensor, outermost first; the innermost
+ * dimension (DI, DQ or DV) is always contiguous:
+ *   q_idx [B, T_q, HI, DI]  -> q[0..2]  = batch, row, head strides
+ *   k_idx [B, T_k, DI]      -> k[0..1]  = batch, row
+ *   w_idx [B, T_q, HI]      -> w[0..1]  = batch, row (heads contiguous)
+ *   Q     [B, T_q, HQ, DQ]  -> Q[0..2]  = batch, row, head
+ *   K, V  [B, T_k, HQ, D]   -> K[0..2], V[0..2]
+ * A batch stride may be 0 (every batch reads the same tensor).  For example
+ * K and V sliced out of a fused [B, T, 3, HQ, D] projection have row stride
+ * 3*HQ*D and head stride D; no copy is needed.
+ *
+ * row_bstep: batch b's query rows sit at absolute positions
+ * q_row0 + b*row_bstep + i (i < T_q); 0 in the plain contiguous case.  With
+ * key-side batch strides of 0 this runs several row blocks of ONE sequence
+ * in one launch, e.g. the two zig-zag blocks r and 2N-1-r that a GPU owns when
+ * a sequence's query rows are split across N GPUs: B = 2, T_q = block rows,
+ * q_row0 = r*T_q, row_bstep = (2N-1-2r)*T_q.
+ *
+ * The outputs (scores, O, thresholds, lists, bitmaps) stay contiguous.  Byte
+ * strides that are not multiples of 16 run on the CUDA-core / gather kernels
+ * instead of the tensor-core ones.  No counterpart in the reference, whose
+ * Triton kernels take strides per tensor (lightning_indexer.py:116-124,
+ * dsa_attention.py:313-323) but run one contiguous sequence per batch.
+ */
+typedef struct dsa_layout {
+    int64_t q[3], k[2], w[2], Q[3], K[3], V[3];
+    int64_t row_bstep;
+} dsa_layout;
+
+/* The contiguous layout of the shapes given (row_bstep 0). */
+DSA_API void dsa_layout_contiguous(dsa_layout* out, int64_t T_q, int64_t T_k, int64_t HI,
+                                   int64_t DI, int64_t HQ, int64_t DQ, int64_t DV);
+
 /* Library version, (major << 16) | minor. */
 DSA_API int dsa_version(void);
 
@@ -98,6 +136,13 @@ DSA_API int dsa_indexer_scores(const void* q, const void* k, const float* w, flo
                        int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
                        int64_t HI, int64_t DI, int dtype, int fill_upper, void* stream);
 
+/* dsa_indexer_scores over strided q/k/w and row blocks (layout may be NULL:
+ * contiguous).  Only layout->q, k, w and row_bstep are read. */
+DSA_API int dsa_indexer_scores_ex(const void* q, const void* k, const float* w, float* scores,
+                                  int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                                  int64_t HI, int64_t DI, int dtype, int fill_upper,
+                                  const dsa_layout* layout, void* stream);
+
 /*
  * Stage 2 — per-row top-K threshold and kept-index list (radix select).
  *   scores   n_rows rows of row_len fp32, row r at scores + r*row_stride
@@ -115,6 +160,17 @@ DSA_API int dsa_topk_select(const float* scores, int64_t n_rows, int64_t row_len
                     int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
                     float* thr_out, int32_t* idx_out, int32_t* cnt_out, int64_t idx_cap,
                     void* stream);
+
+/* dsa_topk_select with row blocks and an optional bitmap: causal row r is
+ * query t = q_row0 + (r / rows_per_batch)*row_bstep + r % rows_per_batch.
+ * bits (may be NULL) receives the kept-set bitmap of dsa_kept_bitmap
+ * (requires row_stride == row_len).  NaN scores rank above +inf, as in
+ * torch.topk, and are never kept (score >= thr is false for NaN). */
+DSA_API int dsa_topk_select_ex(const float* scores, int64_t n_rows, int64_t row_len,
+                               int64_t row_stride, int64_t rows_per_batch, int64_t q_row0,
+                               int64_t row_bstep, int causal, int64_t k, float* thr_out,
+                               int32_t* idx_out, int32_t* cnt_out, int64_t idx_cap,
+                               uint32_t* bits, int64_t words_per_row, void* stream);
 
 /*
  * Stage 3 (threshold form) — attention of each query over the keys s <= t
@@ -144,6 +200,16 @@ DSA_API int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_
                     int64_t HQ, int64_t DQ, int64_t DV, float scale,
                     int dtype, void* stream);
 
+/* dsa_sparse_attn (idx != NULL) or dsa_sparse_attn_threshold (idx == NULL)
+ * over strided Q/K/V and row blocks (layout may be NULL: contiguous).  Only
+ * layout->Q, K, V and row_bstep are read. */
+DSA_API int dsa_sparse_attn_ex(const int32_t* idx, const int32_t* cnt, int64_t idx_cap,
+                               const float* scores, const float* thr,
+                               const void* Q, const void* K, const void* V, float* O,
+                               int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                               int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                               int dtype, const dsa_layout* layout, void* stream);
+
 /*
  * Stage 3 (bitmap form, tensor cores) — the kept set as one bit per
  * (query row, key), then a masked flash attention over it.
@@ -155,8 +221,9 @@ DSA_API int dsa_sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_
  *   dsa_sparse_attn_bitmap: attention of each query over its set bits,
  *     O [B, T_q, HQ, DV] fp32 out; Q/K/V as in dsa_sparse_attn_threshold.
  *     bf16 or fp16 with DQ == DV in {64, 128}, else DSA_ERR_UNSUPPORTED.
- *     The softmax weights enter the P.V product rounded to the input dtype;
- *     results agree with the fp32 threshold form to the dtype's tolerance.
+ *     The softmax weights enter the P.V product rounded to the input dtype
+ *     (this entry point has no workspace for an fp16 copy of V; the _ex form
+ *     and dsa_forward use fp16 weights for bf16 inputs too).
  */
 DSA_API int64_t dsa_bitmap_words(int64_t T_k);
 
@@ -179,6 +246,26 @@ DSA_API int dsa_sparse_attn_bitmap(const uint32_t* bits, int64_t words_per_row,
                                    int64_t HQ, int64_t DQ, int64_t DV, float scale,
                                    int dtype, void* stream);
 
+/* dsa_sparse_attn_bitmap over strided Q/K/V and row blocks (layout may be
+ * NULL).  Only layout->Q, K, V and row_bstep are read.  With a workspace of
+ * dsa_sparse_attn_bitmap_workspace_bytes(...) bytes (256-byte aligned):
+ *   - a summary of the bitmap (one bit per 128-row query tile and 128-key
+ *     block) lets the kernel skip key blocks no row of a tile keeps; the
+ *     result is bit-identical to processing every causal block;
+ *   - bf16 inputs: V is copied to fp16 (scaled by a power of two) and the
+ *     softmax weights enter P.V in fp16, whose 11-bit significand keeps the
+ *     output within 1e-3 + 2e-2|O| of the fp32 reference elementwise.
+ * Without one (and in dsa_sparse_attn_bitmap) every causal block is
+ * processed and the weights enter in the input type. */
+DSA_API size_t dsa_sparse_attn_bitmap_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t HQ,
+                                                      int64_t DV, int dtype);
+DSA_API int dsa_sparse_attn_bitmap_ex(const uint32_t* bits, int64_t words_per_row,
+                                      const void* Q, const void* K, const void* V, float* O,
+                                      int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                                      int64_t HQ, int64_t DQ, int64_t DV, float scale,
+                                      int dtype, const dsa_layout* layout, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /*
  * Whole forward (stage 1 -> 2 -> 3) in caller-provided workspace.
  * idx_dtype is the dtype of q_idx/k_idx, qkv_dtype that of Q/K/V; w_idx is fp32.
@@ -192,12 +279,35 @@ DSA_API int dsa_sparse_attn_bitmap(const uint32_t* bits, int64_t words_per_row,
  */
 DSA_API size_t dsa_forward_workspace_bytes(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k);
 
+/* Workspace for dsa_forward / dsa_forward_ex that also holds stage 3's
+ * workspace on the tensor cores (dsa_sparse_attn_bitmap_ex: the block
+ * summary, and for bf16 Q/K/V the fp16 copy of V).  Equal to
+ * dsa_forward_workspace_bytes whenever that fits over the score region,
+ * roughly T_q * (T_k + list capacity) * 4 >= T_k * HQ * DV * 2 (every full
+ * sequence of the reference's configurations); with only
+ * dsa_forward_workspace_bytes for shorter row blocks, stage 3 runs without
+ * block skipping and with bf16 weights. */
+DSA_API size_t dsa_forward_workspace_bytes_ex(int64_t B, int64_t T_q, int64_t T_k, int64_t top_k,
+                                              int64_t HQ, int64_t DV, int qkv_dtype);
+
 DSA_API int dsa_forward(const void* q_idx, const void* k_idx, const float* w_idx,
                 const void* Q, const void* K, const void* V, float* O,
                 int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
                 int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV, int64_t top_k,
                 int idx_dtype, int qkv_dtype, void* workspace, size_t workspace_bytes,
                 void* stream);
+
+/* dsa_forward over strided inputs and row blocks (layout may be NULL:
+ * contiguous).  Same workspace size as dsa_forward.  The GPU that owns
+ * zig-zag blocks r and 2N-1-r of one sequence runs both in one call per
+ * stage: B = 2 with key-side batch strides 0 (see struct dsa_layout). */
+DSA_API int dsa_forward_ex(const void* q_idx, const void* k_idx, const float* w_idx,
+                           const void* Q, const void* K, const void* V, float* O,
+                           int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                           int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV,
+                           int64_t top_k, int idx_dtype, int qkv_dtype,
+                           const dsa_layout* layout, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
 /*
  * Whole forward with no allocation and no caller workspace.  No counterpart
@@ -212,7 +322,9 @@ DSA_API int dsa_forward(const void* q_idx, const void* k_idx, const float* w_idx
  *   DSA_ERR_INVALID (e.g. B=16, T=512, top_k=32 fits; T=8192 does not).
  *   The first call on a device looks up the array's device address for that
  *   device (cudaGetSymbolAddress); make that first call before any stream
- *   capture.  No cudaMalloc / cudaFree is ever called.
+ *   capture.  The address is looked up again when the device's context has
+ *   changed since (e.g. after cudaDeviceReset).  No cudaMalloc / cudaFree is
+ *   ever called.  An empty call (B*T_q == 0) returns DSA_OK, as dsa_forward.
  *   All calls on a device share the one array and nothing in it needs
  *   clearing between calls; calls that overlap on the GPU (different streams,
  *   or host threads without ordering) race on it and must be serialised.

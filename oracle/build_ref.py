@@ -30,10 +30,13 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
 MOD_NAME = "topk_avx512_ref"
-DEFAULT_REFERENCE = os.environ.get("DSA_REFERENCE_DIR", "/root/reference")
-
-
-def build(reference_dir: str = DEFAULT_REFERENCE, verbose: bool = False) -> str | None:
+def build(reference_dir: str | None = None, verbose: bool = False) -> str | None:
+    """Compile the reference's topk_avx512.cpp found in ``reference_dir`` (or
+    $DSA_REFERENCE_DIR); returns the built module's path, or None when neither
+    names a directory holding the source."""
+    reference_dir = reference_dir or os.environ.get("DSA_REFERENCE_DIR")
+    if not reference_dir:
+        return None
     src = os.path.join(reference_dir, "topk_avx512.cpp")
     if not os.path.exists(src):
         return None
@@ -83,5 +86,5 @@ def load_ref():
 
 
 if __name__ == "__main__":
-    out = build(sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REFERENCE, verbose=True)
-    print(out or "reference sources not found; nothing built")
+    out = build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True)
+    print(out or "usage: build_ref.py <reference checkout> (or set DSA_REFERENCE_DIR); nothing built")

@@ -16,9 +16,11 @@
  *
  * The threshold is the k-th largest element of the row as a multiset
  * (k counted from 1, largest first), i.e. exactly the value torch.topk
- * returns at position k-1.  It is found by quickselect, which gives the same
- * value as any other exact selection.  Floats are compared with the C
- * operators, so -0.0 == +0.0 and -inf sorts last, as in torch.
+ * returns at position k-1.  It is found by quickselect over an ordering key
+ * that follows torch.topk's value order: -0.0 == +0.0, -inf last, and every
+ * NaN above +inf (all NaNs equal).  The kept set then uses the float
+ * comparison scores >= thr of the reference, so a NaN is never kept and a
+ * NaN threshold keeps nothing.
  *
  * Causal rows: query row r of a batch of `rows_per_batch` rows sits at
  * position t = q_row0 + r % rows_per_batch; entries s > t count as -inf
@@ -32,25 +34,34 @@
 
 static void swapf(float* a, float* b) { float t = *a; *a = *b; *b = t; }
 
-/* k-th largest (1-based) of buf[0..n), n >= k >= 1.  Reorders buf. */
+/* torch.topk's order as a total order on floats: NaN (any sign or payload)
+ * above +inf, -0.0 equal to +0.0, everything else by value. */
+static int gt(float a, float b) {
+    if (isnan(a)) return !isnan(b);
+    if (isnan(b)) return 0;
+    return a > b;
+}
+static int lt(float a, float b) { return gt(b, a); }
+
+/* k-th largest (1-based) of buf[0..n), n >= k >= 1, in gt/lt order.  Reorders buf. */
 static float kth_largest(float* buf, int64_t n, int64_t k) {
     int64_t lo = 0, hi = n - 1, want = k - 1; /* index in descending order */
     while (lo < hi) {
         /* median of three, pivot moved to hi */
         int64_t mid = lo + (hi - lo) / 2;
-        if (buf[mid] > buf[lo]) swapf(&buf[mid], &buf[lo]);
-        if (buf[hi] > buf[lo]) swapf(&buf[hi], &buf[lo]);
-        if (buf[mid] > buf[hi]) swapf(&buf[mid], &buf[hi]);
+        if (gt(buf[mid], buf[lo])) swapf(&buf[mid], &buf[lo]);
+        if (gt(buf[hi], buf[lo])) swapf(&buf[hi], &buf[lo]);
+        if (gt(buf[mid], buf[hi])) swapf(&buf[mid], &buf[hi]);
         float p = buf[hi];
         /* three-way partition, descending: [> p | == p | < p] */
-        int64_t gt = lo, i = lo, lt = hi;
-        while (i <= lt) {
-            if (buf[i] > p) { swapf(&buf[i], &buf[gt]); gt++; i++; }
-            else if (buf[i] < p) { swapf(&buf[i], &buf[lt]); lt--; }
+        int64_t g = lo, i = lo, l = hi;
+        while (i <= l) {
+            if (gt(buf[i], p)) { swapf(&buf[i], &buf[g]); g++; i++; }
+            else if (lt(buf[i], p)) { swapf(&buf[i], &buf[l]); l--; }
             else i++;
         }
-        if (want < gt) hi = gt - 1;
-        else if (want > lt) lo = lt + 1;
+        if (want < g) hi = g - 1;
+        else if (want > l) lo = l + 1;
         else return p;
     }
     return buf[lo];

@@ -136,4 +136,7 @@ def main(ref_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DSA_REFERENCE_DIR")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference checkout> (or set DSA_REFERENCE_DIR)")
+    main(ref)

@@ -3,8 +3,8 @@ flash attention) against the oracle.
 
 The bitmap is integer work and must match bit for bit.  The attention rounds
 its softmax weights to the input dtype before the P.V product, so it is held
-to the north-star bf16/fp16 tolerance (2e-2 relative to max(1, |O|max)), and
-it is also compared with the fp32 gather kernel on identical kept sets."""
+to the north-star bf16/fp16 tolerance elementwise (|err| <= 1e-3 + 2e-2 |ref|),
+and it is also compared with the fp32 gather kernel on identical kept sets."""
 import math
 
 import numpy as np
@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import dsa_oracle as o
+from conftest import assert_close_elementwise
 
 pytestmark = pytest.mark.gpu
 
@@ -81,8 +82,7 @@ def test_bitmap_and_tc_attention_match_oracle(cuda, B, T_q, T_k, HQ, D, k, dtype
     out = sparse_attention_with_bitmap(bits, Q.to(cuda), K.to(cuda), V.to(cuda), q_row0=q_row0).cpu()
     ref = _oracle(sc, thr, Q, K, V, q_row0)
     assert torch.isfinite(out).all()
-    err = (out - ref).abs().max().item()
-    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), err
+    assert_close_elementwise(out, ref, what="tensor-core attention vs oracle")
 
 
 def test_tc_attention_agrees_with_gather_kernel(cuda, monkeypatch):
@@ -93,7 +93,7 @@ def test_tc_attention_agrees_with_gather_kernel(cuda, monkeypatch):
     tc = sparse_attention_with_threshold_triton(*args)
     monkeypatch.setenv("DSA_ATTN_GATHER", "1")
     ga = sparse_attention_with_threshold_triton(*args)
-    assert (tc - ga).abs().max().item() <= 2e-2
+    assert_close_elementwise(tc, ga, what="tensor-core vs gather attention")
 
 
 @pytest.mark.parametrize("B,T,HI,DI,HQ,D,k,dtype", [
@@ -106,9 +106,16 @@ def test_forward_tc_path_matches_oracle_and_gather(cuda, B, T, HI, DI, HQ, D, k,
     out = dsa_forward(*args, k)
     monkeypatch.setenv("DSA_ATTN_GATHER", "1")
     ga = dsa_forward(*args, k)
-    assert (out - ga).abs().max().item() <= 2e-2
-    ref = o.dsa_attention(*(a.cpu() for a in args), k)
-    assert (out.cpu() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    assert_close_elementwise(out, ga, what="forward: tensor-core vs gather stage 3")
+    # the oracle's attention on the GPU's own scores and thresholds (the bf16
+    # indexer's sums round differently from the fp32 oracle's, which can move
+    # a key across a near-tied threshold)
+    from lightning_indexer import indexer_scores
+    from topk import topk_select
+    sc = indexer_scores(*args[:3])
+    thr, _, _ = topk_select(sc, k, causal=True, return_idx=False)
+    ref = o.sparse_attention_with_threshold(sc.cpu(), thr.cpu().view(B, T, 1), *(a.cpu() for a in args[3:]))
+    assert_close_elementwise(out, ref, what="forward vs oracle on the GPU's scores")
 
 
 def test_bitmap_entry_points_reject_bad_arguments(cuda):
@@ -142,7 +149,7 @@ def test_attention_wait_timeout_is_reported_and_recoverable(cuda, monkeypatch):
     out = sparse_attention_with_bitmap(bits, Q, K, V).cpu()
     assert _native.device_status() == _native.DSA_OK
     ref = _oracle(sc, thr, Q.cpu(), K.cpu(), V.cpu(), 0)
-    assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    assert_close_elementwise(out, ref, what="attention after a timeout")
 
 
 @pytest.mark.parametrize("B,T_q,T_k,k,q_row0,causal", [
@@ -245,3 +252,27 @@ def test_row_blocks_of_the_tc_forward_equal_the_whole(cuda):
                          100, q_row0=a)
              for a, b in [(0, 77), (77, 400), (400, 900)]]
     assert torch.equal(torch.cat(parts, 1), whole)
+
+
+@pytest.mark.parametrize("T,window,stride", [(2048, 200, 512), (1500, 64, 300)])
+def test_block_skipping_is_exact_on_structured_selections(cuda, T, window, stride, monkeypatch):
+    """Kept sets of a local window plus strided key blocks (most 128x128 tiles
+    hold no kept key): the attention that skips empty key blocks equals the one
+    that processes every causal block bit for bit, and the oracle elementwise."""
+    from dsa_attention import kept_bitmap, sparse_attention_with_bitmap
+    B, HQ, D, k = 1, 2, 128, 256
+    t = torch.arange(T).view(T, 1)
+    s = torch.arange(T).view(1, T)
+    g = torch.Generator().manual_seed(T)
+    sc = torch.randn(1, T, T, generator=g) * 0.1
+    sc += ((t - s >= 0) & (t - s < window)).float() * 10 + ((s % stride) < 64).float() * 5
+    thr = sc.masked_fill(s > t, float("-inf")).topk(k, dim=-1).values[..., -1]
+    thr = torch.where(torch.isfinite(thr), thr, torch.full_like(thr, float("-inf")))
+    Q, K, V = (torch.randn(B, T, HQ, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    bits = kept_bitmap(sc.to(cuda), thr.to(cuda))
+    args = (bits, Q.to(cuda), K.to(cuda), V.to(cuda))
+    skipped = sparse_attention_with_bitmap(*args)
+    monkeypatch.setenv("DSA_ATTN_NO_SKIP", "1")
+    full = sparse_attention_with_bitmap(*args)
+    assert torch.equal(skipped, full)
+    assert_close_elementwise(skipped, _oracle(sc, thr, Q, K, V, 0), what="structured selection vs oracle")

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, golden, t
+from conftest import GOLDEN, assert_close_elementwise, golden, t
 import dsa_oracle as o
 
 pytestmark = pytest.mark.gpu
@@ -32,14 +32,25 @@ def test_forward_matches_reference_golden(cuda, name):
     args, dt = inputs(d, cuda)
     k = int(d["top_k"])
     ref = t(d["out"])
-    tol = 5e-4 if dt == torch.float32 else 2e-2
-    for fn in (dsa_attention_split_triton, dsa_attention_triton):
-        out = fn(*args, top_k=k).cpu()
+
+    def check(out, what):
         assert out.dtype == torch.float32 and out.shape == ref.shape
-        assert (out - ref).abs().max() < tol, fn.__name__
+        if dt == torch.float32:
+            assert (out - ref).abs().max() < 5e-4, what   # the reference tests' bar (test_dsa.py:41)
+        else:
+            # The reference's torch variant ran this case in bf16 arithmetic: its
+            # einsums round every head's dot product and every logit to bf16 and
+            # its output is a bf16 tensor (half an ulp is 4e-3 at |O| = 1), so
+            # the golden carries bf16 errors of its own.  The bar here is rtol
+            # 2e-2 with atol 2e-2; the checks against the fp32 oracle on
+            # identical kept sets (test_threshold_form_matches_oracle,
+            # test_forward_random, test_full_size_gpu) use atol 1e-3.
+            assert_close_elementwise(out, ref, atol=2e-2, what=f"{name} {what}")
+
+    for fn in (dsa_attention_split_triton, dsa_attention_triton):
+        check(fn(*args, top_k=k).cpu(), fn.__name__)
     ctx = HybridContext(*args[3].shape[:2])
-    out = dsa_hybrid_cpu_topk(*args, top_k=k, ctx=ctx).cpu()
-    assert (out - ref).abs().max() < tol
+    check(dsa_hybrid_cpu_topk(*args, top_k=k, ctx=ctx).cpu(), "dsa_hybrid_cpu_topk")
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -49,7 +60,7 @@ def test_threshold_form_matches_oracle(cuda, name, monkeypatch):
     The gather kernel computes in fp32 on the upcast inputs like the
     reference (1e-4 fp32, 1e-3 bf16).  For bf16 heads of 64/128 the default
     path is the tensor-core kernel, which rounds the softmax weights to bf16
-    before P.V: it is held to the bf16 bar, 2e-2 of max(1, |O|)."""
+    before P.V: it is held to the bf16 bar elementwise, 1e-3 + 2e-2 |O|."""
     import _native
     from dsa_attention import sparse_attention_with_threshold_triton
     d = golden(name)
@@ -58,9 +69,10 @@ def test_threshold_form_matches_oracle(cuda, name, monkeypatch):
     thr = t(d["thr"])
     ref = o.sparse_attention_with_threshold(sc, thr, *(a.cpu() for a in args[3:]))
     out = sparse_attention_with_threshold_triton(sc.to(cuda), thr.to(cuda), *args[3:]).cpu()
-    tc = _native.attn_tc_supported(args[3], args[5])
-    tol = 2e-2 * max(1.0, ref.abs().max().item()) if tc else (1e-4 if dt == torch.float32 else 1e-3)
-    assert (out - ref).abs().max() < tol
+    if _native.attn_tc_supported(args[3], args[5]):
+        assert_close_elementwise(out, ref, what=f"{name} tensor-core threshold form")
+    else:
+        assert (out - ref).abs().max() < (1e-4 if dt == torch.float32 else 1e-3)
     monkeypatch.setenv("DSA_ATTN_GATHER", "1")
     out = sparse_attention_with_threshold_triton(sc.to(cuda), thr.to(cuda), *args[3:]).cpu()
     assert (out - ref).abs().max() < (1e-4 if dt == torch.float32 else 1e-3)
@@ -97,7 +109,7 @@ def test_forward_random(cuda, B, T, HI, DI, HQ, D, k, dtype, monkeypatch):
 
     The elementwise bounds hold for the fp32-arithmetic gather kernel.  bf16/fp16
     heads of 64/128 also run the default tensor-core stage 3, whose bf16 softmax
-    weights are held to 2e-2 of max(1, |O|)."""
+    weights are held to the bf16 bar elementwise (1e-3 + 2e-2 |O|)."""
     import _native
     from dsa_attention import dsa_forward
     from lightning_indexer import indexer_scores
@@ -122,7 +134,7 @@ def test_forward_random(cuda, B, T, HI, DI, HQ, D, k, dtype, monkeypatch):
     bad = ((out - ref2).abs() > 1e-3 + rtol * ref2.abs()).any(-1).any(-1)
     assert bad.float().mean() < 0.002, "rows differing from the independent oracle"
     if tc_out is not None:
-        assert (tc_out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+        assert_close_elementwise(tc_out, ref, what="tensor-core forward vs oracle on the GPU's scores")
 
 
 def test_row_sharded_forward_equals_whole(cuda):

@@ -7,10 +7,11 @@ are checked against the oracle:
     < k, the count at or above it is >= min(k, t+1); the kept list is
     ascending, in 0..t, and holds exactly the positions >= threshold;
   - the kept-set bitmap of every row holds exactly cnt bits;
-  - sampled rows: threshold and kept list bit-exact against the C oracle on
-    the GPU's score row; indexer scores within the bf16 tolerance of the
-    fp32 oracle; attention output within tolerance of the oracle run on the
-    GPU's kept set; and the pipeline's output equals the stage-by-stage one.
+  - 64 sampled rows stratified over every batch: threshold and kept list
+    bit-exact against the C oracle on the GPU's score row; indexer scores
+    within the bf16 tolerance of the fp32 oracle; attention output within
+    1e-3 + 2e-2 |O| elementwise of the oracle run on the GPU's kept set;
+    and the pipeline's output equals the stage-by-stage one.
 """
 import math
 
@@ -19,6 +20,7 @@ import pytest
 import torch
 
 import dsa_oracle as o
+from conftest import ATOL_16, assert_close_elementwise
 
 pytestmark = pytest.mark.gpu
 
@@ -87,30 +89,37 @@ def test_forward_full_size(cuda, name):
     asc = il[:, 1:] > il[:, :-1]
     assert bool((asc | ~valid[:, 1:]).all())
 
-    # ---- sampled rows against the oracle
-    picks = [0, 1, k - 2, k - 1, k, T // 2, T - 2, T - 1]
-    b_pick = B - 1
-    sc_rows = sc[b_pick, picks].cpu()
-    cpu = [x[b_pick:b_pick + 1].cpu() for x in args]
-    # the oracle's causal rule needs each row's absolute position: row by row
-    for j, tt in enumerate(picks):
-        th1, id1, c1 = o.topk_select(sc_rows[j:j + 1], k, causal=True, rows_per_batch=1, q_row0=tt,
-                                     idx_cap=cap)
-        r = b_pick * T + tt
-        assert th1[0] == thr[r].item()
-        assert c1[0] == cnt[r].item()
-        m = min(int(c1[0]), cap)
-        assert np.array_equal(id1[0, :m], idx[r, :m].cpu().numpy())
-        # indexer scores of the row vs the fp32 oracle (bf16 inputs upcast)
-        ref = o.indexer_scores(*cpu[:3], slice(tt, tt + 1))[0, 0, : tt + 1]
-        got = sc_rows[j, : tt + 1]
-        mag = (cpu[0][0, tt].float().abs() @ cpu[1][0, : tt + 1].float().abs().T).mean().item()
-        assert bool(((got - ref).abs() <= 2e-2 * ref.abs() + 1e-3 * mag).all())
-        # attention of the row over the GPU's kept set (threshold form if the list overflowed)
-        if int(cnt[r]) <= cap:
-            oo = o.attention_from_lists(idx[r].cpu().numpy(), int(cnt[r]), *cpu[3:], 0, tt)
-        else:
-            oo = o.sparse_attention_with_threshold(sc[b_pick:b_pick + 1, tt:tt + 1].cpu(),
-                                                   thr[r:r + 1].cpu().view(1, 1, 1), *cpu[3:],
-                                                   rows=slice(tt, tt + 1))[0, 0]
-        assert (O[b_pick, tt].cpu() - oo).abs().max().item() <= 2e-2 * max(1.0, oo.abs().max().item())
+    # ---- sampled rows against the oracle: 64 rows stratified over every batch
+    # (the edges of the causal ramp and evenly spaced positions between them)
+    per_b = max(16, 64 // B)
+    edges = [0, 1, k - 2, k - 1, k, T - 2, T - 1]
+    spread = np.linspace(2, T - 3, per_b - len(edges)).round().astype(int).tolist()
+    picks = sorted(set(edges + spread))
+    rels = []
+    for b_pick in range(B):
+        sc_rows = sc[b_pick, picks].cpu()
+        cpu = [x[b_pick:b_pick + 1].cpu() for x in args]
+        # the oracle's causal rule needs each row's absolute position: row by row
+        for j, tt in enumerate(picks):
+            th1, id1, c1 = o.topk_select(sc_rows[j:j + 1], k, causal=True, rows_per_batch=1, q_row0=tt,
+                                         idx_cap=cap)
+            r = b_pick * T + tt
+            assert th1[0] == thr[r].item()
+            assert c1[0] == cnt[r].item()
+            m = min(int(c1[0]), cap)
+            assert np.array_equal(id1[0, :m], idx[r, :m].cpu().numpy())
+            # indexer scores of the row vs the fp32 oracle (bf16 inputs upcast)
+            ref = o.indexer_scores(*cpu[:3], slice(tt, tt + 1))[0, 0, : tt + 1]
+            got = sc_rows[j, : tt + 1]
+            mag = (cpu[0][0, tt].float().abs() @ cpu[1][0, : tt + 1].float().abs().T).mean().item()
+            assert bool(((got - ref).abs() <= 2e-2 * ref.abs() + 1e-3 * mag).all())
+            # attention of the row over the GPU's kept set (threshold form if the list overflowed)
+            if int(cnt[r]) <= cap:
+                oo = o.attention_from_lists(idx[r].cpu().numpy(), int(cnt[r]), *cpu[3:], 0, tt)
+            else:
+                oo = o.sparse_attention_with_threshold(sc[b_pick:b_pick + 1, tt:tt + 1].cpu(),
+                                                       thr[r:r + 1].cpu().view(1, 1, 1), *cpu[3:],
+                                                       rows=slice(tt, tt + 1))[0, 0]
+            rels.append(assert_close_elementwise(O[b_pick, tt], oo, what=f"{name} row b={b_pick} t={tt}"))
+    print(f"{name}: {len(rels)} sampled rows, max relative error of O {max(rels):.3e} "
+          f"(|O| floored at {ATOL_16:g})")
