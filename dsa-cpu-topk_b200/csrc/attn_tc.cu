@@ -19,7 +19,7 @@
 // 128-row query tile, head); units are dealt longest first:
 //   warp 0      TMA producer: the unit's Q tile once, then per key block
 //               K[s0:s0+128, h, :] and V[s0:s0+128, h, :] (128-byte swizzle,
-//               no multicast) through two mbarrier rings
+//               each CTA loads its own tiles) through two mbarrier rings
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T (M=128, N=128) into one
 //               of two TMEM buffers, one block ahead of the softmax; then
 //               O += P_j V_j (M=128, N=D, V read MN-major) into a TMEM

@@ -1,5 +1,5 @@
 // PTX wrappers shared by the tcgen05 kernels (indexer_tc.cu, attn_tc.cu):
-// mbarriers with bounded waits, TMA tile loads (no multicast), shared-memory
+// mbarriers with bounded waits, TMA tile loads (each CTA its own), shared-memory
 // matrix descriptors, tcgen05.mma / commit / fences, and TMEM loads/stores.
 // Everything is hand-written inline PTX for sm_100a.
 #pragma once
@@ -280,7 +280,7 @@ inline EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Tiled map (128-byte swizzle unless given), zero fill out of bounds (no multicast use).
+// Tiled map (128-byte swizzle unless given), zero fill out of bounds.
 inline int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
                       const cuuint64_t* strides, const cuuint32_t* box, const std::string& what,
                       CUtensorMapDataType dt, CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
