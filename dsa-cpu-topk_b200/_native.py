@@ -90,13 +90,15 @@ def lib() -> ctypes.CDLL:
         L.dsa_forward_workspace_bytes_ex.restype = sz
         L.dsa_forward_ex.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                      i32, i32, lp, p, sz, p]
+        L.dsa_quantize_fp8_rows.argtypes = [p, i32, i64, i64, i64, p, p, p]
+        L.dsa_indexer_scores_fp8.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i64, i64, i32, lp, p]
         L.dsa_forward_noalloc.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                           i64, i32, i32, p]
         for name in ("dsa_indexer_scores", "dsa_topk_select", "dsa_sparse_attn_threshold",
                      "dsa_sparse_attn", "dsa_forward", "dsa_kept_bitmap", "dsa_sparse_attn_bitmap",
                      "dsa_topk_select_bitmap", "dsa_indexer_scores_ex", "dsa_topk_select_ex",
                      "dsa_sparse_attn_ex", "dsa_sparse_attn_bitmap_ex", "dsa_forward_ex",
-                     "dsa_forward_noalloc"):
+                     "dsa_forward_noalloc", "dsa_quantize_fp8_rows", "dsa_indexer_scores_fp8"):
             getattr(L, name).restype = i32
         _lib = L
     return _lib
@@ -310,3 +312,21 @@ def forward_noalloc(q_idx, k_idx, w_idx, Q, K, V, O, top_k, *, q_row0=0):
     _check(lib().dsa_forward_noalloc(_ptr(q_idx), _ptr(k_idx), _ptr(w_idx), _ptr(Q), _ptr(K), _ptr(V),
                                      _ptr(O), B, T_q, T_k, q_row0, HI, DI, HQ, DQ, DV, top_k,
                                      dtype_code(q_idx), dtype_code(Q), _stream()), "dsa_forward_noalloc")
+
+
+def quantize_fp8_rows(x, out, scale):
+    """Rows of x's last dimension -> e4m3 ``out`` and per-row ``scale`` (max|x| / 448)."""
+    D = x.shape[-1]
+    rows = x.numel() // D if D else 0
+    assert x.stride(-1) == 1 and (x.dim() == 1 or x.is_contiguous()), "rows must be contiguous"
+    _check(lib().dsa_quantize_fp8_rows(_ptr(x), dtype_code(x), rows, D, D, _ptr(out), _ptr(scale), _stream()),
+           "dsa_quantize_fp8_rows")
+
+
+def indexer_scores_fp8(q8, k8, w, k_scale, scores, *, q_row0=0, row_bstep=0, fill_upper=True):
+    B, T_q, HI, DI = q8.shape
+    T_k = k8.shape[1]
+    L = layout(q=q8, k=k8, w=w, row_bstep=row_bstep)
+    _check(lib().dsa_indexer_scores_fp8(_ptr(q8), _ptr(k8), _ptr(w), _ptr(k_scale), _ptr(scores), B, T_q, T_k,
+                                        q_row0, HI, DI, int(bool(fill_upper)), ctypes.byref(L), _stream()),
+           "dsa_indexer_scores_fp8")

@@ -468,6 +468,18 @@ __device__ __forceinline__ Unit2 decode_unit2(int u, const AtParams& p) {
 __device__ __forceinline__ bool block_used(const AtParams& p, int b, int qt, int j) {
     return !p.summ || ((__ldg(p.summ + ((int64_t)b * p.n_qt + qt) * p.sw + (j >> 5)) >> (j & 31)) & 1u);
 }
+// Whether every key block 0..n-1 of query tile qt is used (then the walks
+// over a unit's blocks take every block without reading the summary again).
+__device__ __forceinline__ bool tile_full(const AtParams& p, int b, int qt, int n) {
+    if (!p.summ) return true;
+    const uint32_t* w = p.summ + ((int64_t)b * p.n_qt + qt) * p.sw;
+    for (int i = 0; i * 32 < n; ++i) {
+        const int left = n - i * 32;
+        const uint32_t need = left >= 32 ? 0xffffffffu : ((1u << left) - 1u);
+        if ((__ldg(w + i) & need) != need) return false;
+    }
+    return true;
+}
 
 template <bool F16, bool PV16>
 __global__ void __launch_bounds__(NT2, 1)
@@ -566,7 +578,9 @@ __global__ void __launch_bounds__(NT2, 1)
                 };
                 // the unit's key blocks: those either tile uses (all causal ones
                 // without a summary); K runs one used block ahead of V
+                const bool dense = tile_full(p, w.b, w.qa, w.na) && (w.nb == 0 || tile_full(p, w.b, w.qa + 1, w.nb));
                 auto next_used = [&](int j) {
+                    if (dense) return j + 1;
                     do { ++j; } while (j < nblk && !((j < w.na && block_used(p, w.b, w.qa, j)) ||
                                                      (j < w.nb && block_used(p, w.b, w.qa + 1, j))));
                     return j;
@@ -661,8 +675,12 @@ __global__ void __launch_bounds__(NT2, 1)
                 // before V(u_i) over the unit's used blocks u_i; they are taken in
                 // that order.  A block of this tile gets its S (on K) and PV (on
                 // V) MMA; a block only the other tile uses is released.
-                auto mine = [&](int j) { return j < n && block_used(p, w.b, w.qa + x, j); };
+                const bool fullA = tile_full(p, w.b, w.qa, w.na);
+                const bool fullB = w.nb == 0 || tile_full(p, w.b, w.qa + 1, w.nb);
+                const bool full_x = x == 0 ? fullA : fullB;
+                auto mine = [&](int j) { return j < n && (full_x || block_used(p, w.b, w.qa + x, j)); };
                 auto next_used = [&](int j) {
+                    if (fullA && fullB) return j + 1;
                     do { ++j; } while (j < nblk && !((j < w.na && block_used(p, w.b, w.qa, j)) ||
                                                      (j < w.nb && block_used(p, w.b, w.qa + 1, j))));
                     return j;
@@ -728,7 +746,9 @@ __global__ void __launch_bounds__(NT2, 1)
             const uint32_t* brow = p.bits + ((int64_t)w.b * p.T_q + (row_ok ? tq : 0)) * p.words;
             float m_run = kNegInf, l = 0.f;
             // this tile's key blocks (those holding a kept key of the tile)
+            const bool full = tile_full(p, w.b, qt, nblk);
             auto next_mine = [&](int j) {
+                if (full) return j + 1;
                 do { ++j; } while (j < nblk && !block_used(p, w.b, qt, j));
                 return j;
             };

@@ -13,10 +13,12 @@ namespace dsa {
 // defined in the stage files
 int indexer_scores_simt(const void* q, const void* k, const float* w, float* scores, int64_t B,
                         int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                        int dtype, int fill_upper, const dsa_layout& L, cudaStream_t stream);
+                        int dtype, int fill_upper, const dsa_layout& L, const float* kscale,
+                        cudaStream_t stream);
 int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                      int fill_upper, int dtype, const dsa_layout& L, cudaStream_t stream);
+                      int fill_upper, int dtype, const dsa_layout& L, const float* kscale,
+                      cudaStream_t stream);
 bool indexer_tc_supported(int64_t HI, int64_t DI, int dtype);
 int indexer_tc_take_timeout(cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
@@ -139,11 +141,11 @@ static int check_layout(const dsa_layout& L, const char* what) {
 
 static int run_indexer(const void* q, const void* k, const float* w, float* scores, int64_t B,
                        int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI, int dtype,
-                       int fill_upper, const dsa_layout& L, cudaStream_t st) {
+                       int fill_upper, const dsa_layout& L, cudaStream_t st, const float* kscale = nullptr) {
     if (indexer_tc_supported(HI, DI, dtype) && aligned16(q) && aligned16(k) && aligned16(scores) &&
         aligned16(w) && !force_simt()) {
         const int rc = indexer_scores_tc(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper,
-                                         dtype, L, st);
+                                         dtype, L, kscale, st);
         if (rc == -101) {
             // row blocks too many for one launch's tile table: one launch per batch
             const size_t e = dtype_size(dtype);
@@ -153,14 +155,16 @@ static int run_indexer(const void* q, const void* k, const float* w, float* scor
                 const int r = run_indexer(static_cast<const char*>(q) + b * L.q[0] * e,
                                           static_cast<const char*>(k) + b * L.k[0] * e, w + b * L.w[0],
                                           scores + b * T_q * T_k, 1, T_q, T_k, q_row0 + b * L.row_bstep,
-                                          HI, DI, dtype, fill_upper, Lb, st);
+                                          HI, DI, dtype, fill_upper, Lb, st,
+                                          kscale ? kscale + (L.k[0] == 0 ? 0 : b * T_k) : nullptr);
                 if (r) return r;
             }
             return DSA_OK;
         }
         if (rc != -100) return rc;  // -100: shape beyond the tensor-core kernel's limits
     }
-    return indexer_scores_simt(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper, L, st);
+    return indexer_scores_simt(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper, L, kscale,
+                               st);
 }
 
 }  // namespace dsa
@@ -189,6 +193,20 @@ int dsa_indexer_scores_ex(const void* q, const void* k, const float* w, float* s
     if (B * T_q == 0) return DSA_OK;
     return run_indexer(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, dtype, fill_upper, L,
                        (cudaStream_t)stream);
+}
+
+int dsa_indexer_scores_fp8(const void* q8, const void* k8, const float* w, const float* k_scale,
+                           float* scores, int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                           int64_t HI, int64_t DI, int fill_upper, const dsa_layout* layout, void* stream) {
+    clear_error();
+    int rc = check_indexer_args(q8, k8, w, scores, B, T_q, T_k, q_row0, HI, DI, DSA_FP8_E4M3);
+    if (rc) return rc;
+    const dsa_layout L = layout_or_contiguous(layout, T_q, T_k, HI, DI, 1, 1, 1);
+    if ((rc = check_layout(L, "indexer_scores_fp8"))) return rc;
+    if (B * T_q == 0) return DSA_OK;
+    if (!k_scale) return fail(DSA_ERR_INVALID, "indexer_scores_fp8: k_scale is required");
+    return run_indexer(q8, k8, w, scores, B, T_q, T_k, q_row0, HI, DI, DSA_FP8_E4M3, fill_upper, L,
+                       (cudaStream_t)stream, k_scale);
 }
 
 int dsa_indexer_scores(const void* q, const void* k, const float* w, float* scores, int64_t B,

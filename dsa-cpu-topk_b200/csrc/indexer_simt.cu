@@ -29,6 +29,8 @@ constexpr int BT = 64, BS = 64, DC = 32;
 // the per-batch step of the first query row
 struct SimtLayout {
     int64_t qb, qr, qh, kb, kr, wb, wr, row_bstep;
+    const float* kscale;   // per-key scales [B or 1, T_k] (batch stride ksb), or null
+    int64_t ksb;
 };
 
 template <typename T>
@@ -71,6 +73,9 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
 
     const T* qb = q + b * ly.qb;
     const T* kb = k + b * ly.kb;
+    const float* wrow[4];   // head weights of this thread's four query rows
+#pragma unroll
+    for (int i = 0; i < 4; ++i) wrow[i] = w + b * ly.wb + (tq0 + ty + 16 * i) * ly.wr;
     for (int j = 0; j < HI; ++j) {
         float dot[4][4];
 #pragma unroll
@@ -117,7 +122,7 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int64_t tq = tq0 + ty + 16 * i;
-            const float wv = tq < T_q ? w[b * ly.wb + tq * ly.wr + j] : 0.f;
+            const float wv = tq < T_q ? wrow[i][j] : 0.f;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(wv, fmaxf(dot[i][jj], 0.f), acc[i][jj]);
         }
@@ -132,7 +137,8 @@ __global__ void __launch_bounds__(256) indexer_simt_kernel(const T* __restrict__
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int64_t s = s0 + tx + 16 * jj;
-            if (s < T_k) out[s] = s <= t ? acc[i][jj] : NEG;
+            if (s < T_k)
+                out[s] = s <= t ? (ly.kscale ? acc[i][jj] * __ldg(ly.kscale + b * ly.ksb + s) : acc[i][jj]) : NEG;
         }
     }
 }
@@ -177,14 +183,24 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
     const int HD = HI * DI;
     const T* qb = q + b * ly.qb + tq0 * ly.qr;
     const T* kb = k + b * ly.kb + s0 * ly.kr;
-    for (int e = tid; e < BT * HD; e += 256) {
-        const int r = e / HD, c = e - r * HD;
-        const int hh = c / DI, d = c - hh * DI;
-        qs[r * QS + c] = tq0 + r < T_q ? Elem<T>::to_f(qb[r * ly.qr + hh * ly.qh + d]) : 0.f;
+    if (ly.qh == DI && ly.qr == HD) {   // contiguous rows: linear offsets
+        for (int e = tid; e < BT * HD; e += 256)
+            qs[(e / HD) * QS + e % HD] = tq0 + e / HD < T_q ? Elem<T>::to_f(qb[e]) : 0.f;
+    } else if (ly.qh == DI) {   // heads contiguous within a row: one offset per row
+        for (int e = tid; e < BT * HD; e += 256) {
+            const int r = e / HD, c = e - r * HD;
+            qs[r * QS + c] = tq0 + r < T_q ? Elem<T>::to_f(qb[r * ly.qr + c]) : 0.f;
+        }
+    } else {
+        for (int e = tid; e < BT * HD; e += 256) {
+            const int r = e / HD, c = e - r * HD;
+            const int hh = c / DI, d = c - hh * DI;
+            qs[r * QS + c] = tq0 + r < T_q ? Elem<T>::to_f(qb[r * ly.qr + hh * ly.qh + d]) : 0.f;
+        }
     }
     for (int e = tid; e < BS * DI; e += 256) {
         const int r = e / DI, c = e - r * DI;
-        ks[r * KS + c] = s0 + r < T_k ? Elem<T>::to_f(kb[r * ly.kr + c]) : 0.f;
+        ks[r * KS + c] = s0 + r < T_k ? Elem<T>::to_f(kb[ly.kr == DI ? (int64_t)e : r * ly.kr + c]) : 0.f;
     }
     __syncthreads();
 
@@ -193,6 +209,9 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) acc[i][jj] = 0.f;
+    const float* wrow[4];   // head weights of this thread's four query rows
+#pragma unroll
+    for (int i = 0; i < 4; ++i) wrow[i] = w + b * ly.wb + (tq0 + ty + 16 * i) * ly.wr;
     for (int j = 0; j < HI; ++j) {
         float dot[4][4];
 #pragma unroll
@@ -236,7 +255,7 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int64_t tq = tq0 + ty + 16 * i;
-            const float wv = tq < T_q ? w[b * ly.wb + tq * ly.wr + j] : 0.f;
+            const float wv = tq < T_q ? wrow[i][j] : 0.f;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(wv, fmaxf(dot[i][jj], 0.f), acc[i][jj]);
         }
@@ -250,7 +269,8 @@ __global__ void __launch_bounds__(256) indexer_simt_small_kernel(const T* __rest
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int64_t s = s0 + tx + 16 * jj;
-            if (s < T_k) out[s] = s <= t ? acc[i][jj] : NEG;
+            if (s < T_k)
+                out[s] = s <= t ? (ly.kscale ? acc[i][jj] * __ldg(ly.kscale + b * ly.ksb + s) : acc[i][jj]) : NEG;
         }
     }
 }
@@ -282,8 +302,10 @@ int launch(const void* q, const void* k, const float* w, float* scores, int64_t 
 
 int indexer_scores_simt(const void* q, const void* k, const float* w, float* scores, int64_t B,
                         int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                        int dtype, int fill_upper, const dsa_layout& L, cudaStream_t stream) {
-    const SimtLayout ly{L.q[0], L.q[1], L.q[2], L.k[0], L.k[1], L.w[0], L.w[1], L.row_bstep};
+                        int dtype, int fill_upper, const dsa_layout& L, const float* kscale,
+                        cudaStream_t stream) {
+    const SimtLayout ly{L.q[0], L.q[1], L.q[2], L.k[0], L.k[1], L.w[0], L.w[1], L.row_bstep, kscale,
+                        L.k[0] == 0 ? 0 : T_k};
     switch (dtype) {
         case DSA_F32:
             return launch<float>(q, k, w, scores, B, T_q, T_k, q_row0, HI, DI, fill_upper, ly, stream);

@@ -60,6 +60,7 @@ struct TcParams {
     int HI, DI, B;
     int flat;                   // tile prefix over (batch, query block) pairs (row blocks differ per batch)
     int kshared;                // k has batch stride 0: every batch reads batch 0's keys
+    const float* kscale;        // per-key scales [B (1 if kshared), T_k] multiplying the scores, or null
     int n_tblk, nsb, tiles_per_batch, total_tiles;
     int nA, nB;
     uint32_t a_bytes, b_bytes;
@@ -286,6 +287,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int64_t t = p.q_row0 + b * p.row_bstep + tq;
             const int64_t s0 = (int64_t)j * BN + half * 128;
             const float NEG = -INFINITY;
+            if (p.kscale) {
+                // FP8 keys quantised per row: I[t,s] = k_scale[s] * sum_j w_j ReLU(<q_j, k8_s>)
+                const float* ks = p.kscale + (p.kshared ? 0 : (int64_t)b * p.T_k);
+#pragma unroll
+                for (int c = 0; c < 128; ++c)
+                    acc[c] *= s0 + c < p.T_k ? __ldg(ks + s0 + c) : 0.f;
+            }
             if (p.tma_store) {
                 // Each 32-row x 16-column chunk is written to a shared buffer
                 // (64-byte swizzle: 16-byte unit u of row r sits at unit
@@ -401,8 +409,10 @@ static int encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64
 
 int indexer_scores_tc(const void* q, const void* k, const float* w, float* scores, int64_t B,
                       int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HI, int64_t DI,
-                      int fill_upper, int dtype, const dsa_layout& L, cudaStream_t stream) {
+                      int fill_upper, int dtype, const dsa_layout& L, const float* kscale,
+                      cudaStream_t stream) {
     TcParams p;
+    p.kscale = kscale;
     p.elt = dtype == DSA_FP8_E4M3 ? 1 : 2;
     // tensor-map strides: positive multiples of 16 bytes (a batch stride of 0
     // on k is read as one shared batch)

@@ -51,6 +51,7 @@ struct TopkArgs {
     int64_t words;
     int cache_elems;
     int cand_max;
+    int cand_words;     // words of the candidate bitmap (uncached bitmap rows), multiple of 4
     int vec_ok;
     int64_t row_bstep;  // causal rows of batch bq sit at q_row0 + bq*row_bstep + (row % rows_per_batch)
 };
@@ -498,6 +499,8 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
     uint32_t* cache = reinterpret_cast<uint32_t*>(dyn4);      // cache_elems keys (multiple of 4)
     uint32_t* cand_key = cache + a.cache_elems;               // cand_max
     int32_t* cand_pos = reinterpret_cast<int32_t*>(cand_key + a.cand_max);
+    uint32_t* cbits = reinterpret_cast<uint32_t*>(cand_pos + a.cand_max);   // cand_words
+
     __shared__ __align__(16) uint32_t hist[NB_TOP];
     __shared__ uint32_t wtot[NW];
     __shared__ uint32_t seg_cnt[NW];
@@ -614,46 +617,44 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
             // loop and break tests use the warp's first group (g0 - lane), so
             // whole warps run the shuffles; gw is a multiple of 8, so the 8
             // lanes of a word are all inside or all past it
-            if (!CACHED && plain && d0 >= 4 && d0 <= NB_TOP - 5) {
+            const bool float_path = !CACHED && plain && d0 >= 4 && d0 <= NB_TOP - 5;
+            if (float_path) {
                 // float compares against the bin edges (finite floats here);
                 // positions past `valid` read as -inf, below bin d0
                 const float hi_f = key2f(hi_key), lo_f = key2f(lo);
-                const float4* src4 = reinterpret_cast<const float4*>(src);
-                for (int g0 = tid; g0 - lane < gw; g0 += PIPE * BLOCK) {
-                    float4 xb[PIPE];
+                // Warp w takes chunks of 32 words (1024 positions): lane L reads
+                // position 32*i + L of word i, so one ballot per word gives the
+                // kept bits (above bin d0) and one the candidates (bin d0); lane i
+                // keeps word i and the chunk is stored as one coalesced line.
+                // Words past `valid` (up to the row's word count) come out zero.
+                const int nwords = (int)a.words;
+                constexpr int SW2 = 16;   // loads in flight per lane
+                for (int ch = warp; ch < ((nwords + 31) >> 5); ch += NW) {
+                    const int s0c = ch * 1024;
+                    uint32_t my_ab = 0, my_cb = 0;
+                    if (s0c < valid) {
+#pragma unroll 1
+                        for (int i0 = 0; i0 < 32; i0 += SW2) {
+                            float x[SW2];
 #pragma unroll
-                    for (int u = 0; u < PIPE; ++u) {
-                        const int g = g0 + u * BLOCK;
-                        if (a.vec_ok && 4 * g + 3 < valid) {
-                            xb[u] = __ldg(src4 + g);
-                        } else {
-                            float e[4];
+                            for (int u = 0; u < SW2; ++u) {
+                                const int sp = s0c + (i0 + u) * 32 + lane;
+                                x[u] = sp < valid ? __ldg(src + sp) : __uint_as_float(0xff800000u);
+                            }
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) e[j] = 4 * g + j < valid ? __ldg(src + 4 * g + j) : __uint_as_float(0xff800000u);
-                            xb[u] = make_float4(e[0], e[1], e[2], e[3]);
+                            for (int u = 0; u < SW2; ++u) {
+                                const uint32_t ab = __ballot_sync(0xffffffffu, x[u] >= hi_f);
+                                const uint32_t cb = __ballot_sync(0xffffffffu, x[u] >= lo_f && x[u] < hi_f);
+                                if (lane == i0 + u) {
+                                    my_ab = ab;
+                                    my_cb = cb;
+                                }
+                            }
                         }
                     }
-#pragma unroll
-                    for (int u = 0; u < PIPE; ++u) {
-                        const int g = g0 + u * BLOCK;
-                        if (g - lane >= gw) break;
-                        const float e[4] = {xb[u].x, xb[u].y, xb[u].z, xb[u].w};
-                        uint32_t nib = 0;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) nib |= (uint32_t)(e[j] >= hi_f) << j;
-                        uint32_t wd = nib << (4 * (lane & 7));
-                        wd |= __shfl_xor_sync(0xffffffffu, wd, 1);
-                        wd |= __shfl_xor_sync(0xffffffffu, wd, 2);
-                        wd |= __shfl_xor_sync(0xffffffffu, wd, 4);
-                        if ((lane & 7) == 0 && g < gw) out[g >> 3] = wd;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            if (e[j] >= lo_f && e[j] < hi_f) {
-                                const uint32_t at = atomicAdd(&n_cand, 1u);
-                                cand_key[at] = f2key_raw(e[j]);   // no NaN on this path
-                                cand_pos[at] = 4 * g + j;
-                            }
-                    }
+                    const int wd = ch * 32 + lane;
+                    if (wd < nwords) out[wd] = my_ab;
+                    if (wd < a.cand_words) cbits[wd] = my_cb;
                 }
             } else
             for (int g0 = tid; g0 - lane < gw; g0 += PIPE * BLOCK) {
@@ -687,11 +688,37 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                     }
                 }
             }
-            // words past the causal end
-            for (int wi = (gw >> 3) + tid; wi < (int)a.words; wi += BLOCK) out[wi] = 0u;
+            // words past the causal end (the float path wrote them)
+            if (!float_path)
+                for (int wi = (gw >> 3) + tid; wi < (int)a.words; wi += BLOCK) out[wi] = 0u;
             if (tid == 0) n_keep = 0;
             __syncthreads();
-            const int nc = (int)n_cand;
+            int nc = (int)n_cand;
+            if (float_path) {
+                // The candidate bitmap becomes the candidate list, in ascending
+                // position: each thread takes a run of words, a block scan of
+                // their popcounts places them, and each candidate's score is read
+                // back (from L2) for its key.  No per-candidate atomics.
+                const int nwc = gw >> 3;
+                const int per = (nwc + BLOCK - 1) / BLOCK;
+                const int w0 = tid * per, w1 = w0 + per < nwc ? w0 + per : nwc;
+                uint32_t c = 0;
+                for (int w = w0; w < w1; ++w) c += __popc(cbits[w]);
+                uint32_t tot;
+                uint32_t at = block_excl_scan<BLOCK>(c, wtot, &tot);
+                for (int w = w0; w < w1; ++w) {
+                    uint32_t m = cbits[w];
+                    while (m) {
+                        const int pos = w * 32 + __ffs(m) - 1;
+                        m &= m - 1;
+                        cand_key[at] = f2key_raw(__ldg(src + pos));   // no NaN on this path
+                        cand_pos[at] = pos;
+                        ++at;
+                    }
+                }
+                nc = (int)tot;
+                __syncthreads();
+            }
             const uint32_t above = (uint32_t)a.k - krem;
 #pragma unroll 1
             for (int pass = 1; pass <= 2; ++pass) {
@@ -878,7 +905,9 @@ int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream, int cand_div
     a.cache_elems = CACHED ? (int)((longest + 3) & ~int64_t(3)) : 0;
     const int64_t cm = longest / cand_div;
     a.cand_max = (int)(cm < 256 ? 256 : cm > 4096 ? 4096 : cm);
-    const size_t smem = ((size_t)a.cache_elems + 2 * (size_t)a.cand_max) * sizeof(uint32_t);
+    // uncached rows: a candidate bitmap word per 32 positions (bitmap-only rows)
+    a.cand_words = CACHED ? 0 : (int)(((longest + 127) / 128) * 4);
+    const size_t smem = ((size_t)a.cache_elems + 2 * (size_t)a.cand_max + a.cand_words) * sizeof(uint32_t);
     auto kern = topk_cached_kernel<BLOCK, CACHED>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
@@ -1317,6 +1346,7 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     a.cnt = cnt;
     a.idx_cap = idx ? idx_cap : 0;
     a.bits = nullptr;
+    a.cand_words = 0;
     a.words = words;
     a.vec_ok = (aligned16(scores) && row_stride % 4 == 0) ? 1 : 0;
     // longest row any CTA will see

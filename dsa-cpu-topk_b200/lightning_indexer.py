@@ -22,19 +22,43 @@ are its CPU/oracle path; they are not part of this GPU package.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 import _native
 from topk import topk_select
 
 
+_W_CAT: dict = {}
+
+
+def _concat_weights(W_Q, W_K, W_W):
+    """[W_Q | W_K | W_W] along the output dimension, cached while the three
+    weight tensors are unchanged (same storage and version counter)."""
+    key = tuple((w.data_ptr(), w._version, tuple(w.shape), w.dtype) for w in (W_Q, W_K, W_W))
+    hit = _W_CAT.get(key)
+    if hit is None:
+        _W_CAT.clear()
+        hit = torch.cat([W_Q, W_K, W_W], dim=1).contiguous()
+        _W_CAT[key] = hit
+    return hit
+
+
 def project(h: torch.Tensor, W_Q: torch.Tensor, W_K: torch.Tensor, W_W: torch.Tensor,
             num_heads: int, head_dim: int):
-    """h @ W_Q / W_K / W_W (lightning_indexer.py:36-42); cuBLAS matmuls on the device."""
+    """h @ W_Q / W_K / W_W (lightning_indexer.py:36-42) as ONE cuBLAS GEMM over the
+    concatenated weights; q, k and w are strided views of its output, which the
+    indexer reads in place (no copies).  DSA_PROJECT_SEPARATE=1 runs the three
+    matmuls of the reference instead."""
     B, T, _ = h.shape
-    q = (h @ W_Q).view(B, T, num_heads, head_dim)
-    k = h @ W_K
-    w = h @ W_W
+    if os.environ.get("DSA_PROJECT_SEPARATE") == "1" or not (W_Q.dtype == W_K.dtype == W_W.dtype):
+        return (h @ W_Q).view(B, T, num_heads, head_dim), h @ W_K, h @ W_W
+    HD = num_heads * head_dim
+    out = h @ _concat_weights(W_Q, W_K, W_W)
+    q = out[..., :HD].view(B, T, num_heads, head_dim)
+    k = out[..., HD:HD + head_dim]
+    w = out[..., HD + head_dim:]
     return q, k, w
 
 
@@ -92,3 +116,27 @@ def topk_mask(scores: torch.Tensor, k: int) -> torch.Tensor:
     eq = s == thr
     need = k_eff - gt.sum(-1, keepdim=True)
     return gt | (eq & (eq.cumsum(-1) <= need))
+
+
+def quantize_fp8(x: torch.Tensor):
+    """Per-row e4m3 quantisation of x's last dimension: (x8, scale) with
+    x ~= x8.float() * scale[..., None], scale = max|row| / 448."""
+    x = x.contiguous()
+    x8 = torch.empty(x.shape, device=x.device, dtype=torch.float8_e4m3fn)
+    scale = torch.empty(x.shape[:-1], device=x.device, dtype=torch.float32)
+    _native.quantize_fp8_rows(x, x8, scale)
+    return x8, scale
+
+
+def indexer_scores_fp8(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, q_row0: int = 0,
+                       fill_upper: bool = True) -> torch.Tensor:
+    """The FP8 Lightning Indexer: q [B,T_q,H,d] and k [B,T_k,d] (any float type) are
+    quantised to e4m3 per row; the key scales multiply the score columns and the
+    query scales fold into w.  Same output as indexer_scores up to e4m3 rounding."""
+    q8, q_s = quantize_fp8(q)
+    k8, k_s = quantize_fp8(k)
+    w2 = (w.float() * q_s).contiguous()
+    B, T_q = q.shape[:2]
+    scores = torch.empty((B, T_q, k.shape[1]), device=q.device, dtype=torch.float32)
+    _native.indexer_scores_fp8(q8, k8, w2, k_s.contiguous(), scores, q_row0=q_row0, fill_upper=fill_upper)
+    return scores

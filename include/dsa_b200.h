@@ -144,6 +144,27 @@ DSA_API int dsa_indexer_scores_ex(const void* q, const void* k, const float* w, 
                                   const dsa_layout* layout, void* stream);
 
 /*
+ * FP8 indexer with per-row scales.  No counterpart in the reference (its
+ * Triton indexer is fp32 only, lightning_indexer.py:54-97); the DeepSeek-V3.2
+ * indexer runs q/k in FP8 with scales this way.
+ *   dsa_quantize_fp8_rows: rows of D values (fp32/bf16/fp16, row r at
+ *     x + r*row_stride) -> out_e4m3 [rows, D] = e4m3(x / s) and scale_out[r] = s
+ *     = max|x_r| / 448 (1 for an all-zero row).
+ *   dsa_indexer_scores_fp8: I[b,t,s] = k_scale[b,s] * sum_j w[b,t,j] *
+ *     ReLU(<q8[b,t,j,:], k8[b,s,:]>), s <= t.  q8 / k8 are e4m3 (layouts as in
+ *     dsa_indexer_scores, strides through layout, may be NULL); k_scale is fp32
+ *     [B, T_k] (or [1, T_k] when k's batch stride is 0).  Per-(query, head)
+ *     scales of q are folded into w by the caller: w'[b,t,j] = w[b,t,j] *
+ *     q_scale[b,t,j] (exact for positive scales, since ReLU(c x) = c ReLU(x)).
+ */
+DSA_API int dsa_quantize_fp8_rows(const void* x, int dtype, int64_t rows, int64_t D, int64_t row_stride,
+                                  void* out_e4m3, float* scale_out, void* stream);
+DSA_API int dsa_indexer_scores_fp8(const void* q8, const void* k8, const float* w, const float* k_scale,
+                                   float* scores, int64_t B, int64_t T_q, int64_t T_k, int64_t q_row0,
+                                   int64_t HI, int64_t DI, int fill_upper, const dsa_layout* layout,
+                                   void* stream);
+
+/*
  * Stage 2 — per-row top-K threshold and kept-index list (radix select).
  *   scores   n_rows rows of row_len fp32, row r at scores + r*row_stride
  *   thr_out  [n_rows] fp32 out: the k-th largest value of the row (as

@@ -90,3 +90,23 @@ def test_small_head_simt_kernel_bitwise(cuda, B, T, HI, DI, dtype, monkeypatch):
     monkeypatch.setenv("DSA_INDEXER_SIMT_GENERIC", "1")
     generic = indexer_scores(qi, ki, wi)
     assert torch.equal(small, generic)
+
+
+@pytest.mark.parametrize("dtype,HI,DI,dm", [(torch.float32, 4, 32, 96), (torch.bfloat16, 16, 128, 256)])
+def test_concatenated_projection_matches_separate_matmuls(cuda, dtype, HI, DI, dm, monkeypatch):
+    """project() as one GEMM over [W_Q | W_K | W_W] with strided q/k/w views
+    gives the scores of the reference's three matmuls (lightning_indexer.py:36-42)."""
+    from lightning_indexer import indexer_triton, project
+    g = torch.Generator().manual_seed(HI + DI)
+    B, T = 2, 384
+    h = torch.randn(B, T, dm, generator=g).to(dtype).to(cuda)
+    W = [(torch.randn(dm, n, generator=g) / dm ** 0.5).to(dtype).to(cuda) for n in (HI * DI, DI, HI)]
+    q, k, w = project(h, *W, HI, DI)
+    assert not q.is_contiguous() and not k.is_contiguous()
+    fused = indexer_triton(h, *W, HI, DI)
+    monkeypatch.setenv("DSA_PROJECT_SEPARATE", "1")
+    sep = indexer_triton(h, *W, HI, DI)
+    fin = torch.isfinite(sep)
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    err = (fused[fin] - sep[fin]).abs()
+    assert bool((err <= tol * sep[fin].abs() + tol * sep[fin].abs().mean()).all()), err.max().item()

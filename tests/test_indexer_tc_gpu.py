@@ -120,3 +120,29 @@ def test_fp8_indexer_in_forward(cuda):
     ref = o.dsa_attention(qi8.float(), ki8.float(), wi, Q, K, V, k)
     bad = ((out - ref).abs() > 2e-2 * ref.abs() + 2e-2).any(-1).any(-1)
     assert bad.float().mean() < 0.002
+
+
+@pytest.mark.parametrize("B,T,HI,DI", [(1, 640, 8, 128), (2, 300, 4, 256), (1, 200, 4, 64)])
+def test_fp8_indexer_with_row_scales_matches_dequantised_oracle(cuda, B, T, HI, DI):
+    """Per-row e4m3 quantisation with the key scales applied to the score
+    columns and the query scales folded into w: equal, to fp32 rounding, to the
+    fp32 oracle on the dequantised inputs (products of e4m3 values are exact),
+    on the tensor cores (DI 128/256) and on the CUDA cores (DI 64)."""
+    from lightning_indexer import indexer_scores_fp8, quantize_fp8
+    g = torch.Generator().manual_seed(T + DI)
+    q = (torch.randn(B, T, HI, DI, generator=g) * 3).to(cuda)
+    k = (torch.randn(B, T, DI, generator=g) * 0.01).to(cuda)        # scales far from 1
+    w = (torch.randn(B, T, HI, generator=g) / HI ** 0.5).to(cuda)
+    out = indexer_scores_fp8(q, k, w).cpu()
+    q8, qs = quantize_fp8(q)
+    k8, ks = quantize_fp8(k)
+    assert q8.dtype == torch.float8_e4m3fn and bool((qs > 0).all())
+    qd = (q8.float() * qs[..., None]).cpu()
+    kd = (k8.float() * ks[..., None]).cpu()
+    # e4m3: 3 mantissa bits (relative error <= 2^-4), subnormal steps of 2^-9 * scale
+    assert bool(((qd - q.cpu()).abs() <= 0.0625 * q.cpu().abs() + 2.0 ** -9 * qs.cpu()[..., None]).all())
+    ref = o.indexer_scores(qd, kd, w.cpu())
+    fin = torch.isfinite(ref)
+    assert torch.equal(torch.isfinite(out), fin)
+    scale = ref[fin].abs().mean()
+    assert bool(((out[fin] - ref[fin]).abs() <= 1e-4 * ref[fin].abs() + 1e-5 * scale).all())
