@@ -450,18 +450,39 @@ __device__ __forceinline__ int tile_blocks(int qt, int b, const AtParams& p) {
 }
 
 // unit index -> (batch, head, tile pair); the pairs with the most key blocks first
+// Units in decreasing size (key blocks grow with the tiles' absolute rows):
+// with one row offset for every batch, by pair from the last, then batch and
+// head; with row blocks that do not overlap (row_bstep >= the block's rows),
+// by batch from the last, then pair from the last, then head.
 __device__ __forceinline__ Unit2 decode_unit2(int u, const AtParams& p) {
     Unit2 r;
     const int bh = p.B * p.HQ;
     const int npair = (p.n_qt + 1) >> 1;
-    const int qr = u / bh, rem = u - qr * bh;
-    const int m = npair - 1 - qr;
-    r.b = rem / p.HQ;
-    r.h = rem - r.b * p.HQ;
+    int m;
+    if (p.row_bstep >= p.T_q && p.B > 1) {
+        const int e = u / p.HQ;
+        r.h = u - e * p.HQ;
+        r.b = p.B - 1 - e / npair;
+        m = npair - 1 - (e - (e / npair) * npair);
+    } else {
+        const int qr = u / bh, rem = u - qr * bh;
+        m = npair - 1 - qr;
+        r.b = rem / p.HQ;
+        r.h = rem - r.b * p.HQ;
+    }
     r.qa = 2 * m;
     r.na = tile_blocks(r.qa, r.b, p);
     r.nb = r.qa + 1 < p.n_qt ? tile_blocks(r.qa + 1, r.b, p) : 0;
     return r;
+}
+
+// The k-th unit of this CTA: units are dealt to the CTAs in rounds, forward
+// in even rounds and backward in odd ones ("snake"), so with units in
+// decreasing size a CTA that drew a large unit early draws a small one next.
+// Returns a value >= total when this CTA has no unit in round k.
+__device__ __forceinline__ int snake_unit(int k) {
+    const int G = (int)gridDim.x;
+    return k * G + ((k & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
 }
 
 // Whether key block j holds a kept key of query tile qt (always, without a summary).
@@ -552,7 +573,9 @@ __global__ void __launch_bounds__(NT2, 1)
             int ks = 0, vs = 0;
             uint32_t kph = 0, vph = 0, qph = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+            for (int kr = 0; ok && kr * (int)gridDim.x < total; ++kr) {
+                const int u = snake_unit(kr);
+                if (u >= total) continue;
                 const Unit2 w = decode_unit2(u, p);
                 const int nblk = w.nb > w.na ? w.nb : w.na;
                 if (!(ok = mbar_wait(q_empty, qph ^ 1, &s_abort, p.timeout_ns, flag))) break;
@@ -665,7 +688,9 @@ __global__ void __launch_bounds__(NT2, 1)
                 mbar_arrive(&empty[st]);
                 return true;
             };
-            for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+            for (int kr = 0; ok && kr * (int)gridDim.x < total; ++kr) {
+                const int u = snake_unit(kr);
+                if (u >= total) continue;
                 const Unit2 w = decode_unit2(u, p);
                 const int n = x == 0 ? w.na : w.nb;
                 const int nblk = w.nb > w.na ? w.nb : w.na;
@@ -736,7 +761,9 @@ __global__ void __launch_bounds__(NT2, 1)
         };
         uint32_t G = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+        for (int kr = 0; ok && kr * (int)gridDim.x < total; ++kr) {
+            const int u = snake_unit(kr);
+            if (u >= total) continue;
             const Unit2 w = decode_unit2(u, p);
             const int nblk = x == 0 ? w.na : w.nb;
             if (nblk == 0) continue;
