@@ -75,31 +75,34 @@ struct TcParams {
 // tile index -> (batch, query block, key block) through the prefix of key
 // blocks per query block: per batch when every batch has the same rows,
 // else over all (batch, query block) pairs
+template <bool FLAT>
 __device__ __forceinline__ void decode_tile(int lin, const int* pref, const TcParams& p, int& b,
                                             int& i, int& j) {
-    int r = lin, n = p.n_tblk;
-    if (p.flat) {
-        n = p.B * p.n_tblk;
-    } else {
-        b = lin / p.tiles_per_batch;
-        r = lin - b * p.tiles_per_batch;
-    }
-    int lo = 0, hi = n - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (pref[mid] <= r) lo = mid;
-        else hi = mid - 1;
-    }
-    j = r - pref[lo];
-    if (p.flat) {
+    if constexpr (FLAT) {
+        int lo = 0, hi = p.B * p.n_tblk - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pref[mid] <= lin) lo = mid;
+            else hi = mid - 1;
+        }
+        j = lin - pref[lo];
         b = lo / p.n_tblk;
         i = lo - b * p.n_tblk;
     } else {
+        b = lin / p.tiles_per_batch;
+        const int r = lin - b * p.tiles_per_batch;
+        int lo = 0, hi = p.n_tblk - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pref[mid] <= r) lo = mid;
+            else hi = mid - 1;
+        }
         i = lo;
+        j = r - pref[lo];
     }
 }
 
-template <bool FP8>
+template <bool FP8, bool FLAT>
 __global__ void __launch_bounds__(NTHREADS, 1)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tms, const TcParams p) {
@@ -125,7 +128,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (threadIdx.x == 0) {
         int acc = 0;
-        const int nb = p.flat ? p.B : 1;
+        const int nb = FLAT ? p.B : 1;
         for (int x = 0; x < nb * p.n_tblk; ++x) {
             const int bb = x / p.n_tblk, i = x - bb * p.n_tblk;
             pref[x] = acc;
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             bool ok = true;
             for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
                 int b, i, j;
-                decode_tile(lin, pref, p, b, i, j);
+                decode_tile<FLAT>(lin, pref, p, b, i, j);
                 if (!(ok = mbar_wait(&emptyB[bs], bph ^ 1, &s_abort, p.timeout_ns, &g_indexer_tc_timeout))) break;
                 if (!p.stall) mbar_expect_tx(&fullB[bs], p.b_bytes);
                 for (int c = 0; c < nch && !p.stall; ++c)
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         bool ok = true;
         for (int lin = blockIdx.x; ok && lin < p.total_tiles; lin += gridDim.x) {
             int b, i, j;
-            decode_tile(lin, pref, p, b, i, j);
+            decode_tile<FLAT>(lin, pref, p, b, i, j);
             const int64_t tq = (int64_t)i * BM + row;
             const bool row_ok = tq < p.T_q;
             const float* wrow = p.w + (int64_t)b * p.wb + (row_ok ? tq : 0) * p.wr;
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int64_t t = p.q_row0 + b * p.row_bstep + tq;
             const int64_t s0 = (int64_t)j * BN + half * 128;
             const float NEG = -INFINITY;
-            if (p.kscale) {
+            if (FP8 && p.kscale) {   // compiled out of the bf16 kernel
                 // FP8 keys quantised per row: I[t,s] = k_scale[s] * sum_j w_j ReLU(<q_j, k8_s>)
                 const float* ks = p.kscale + (p.kshared ? 0 : (int64_t)b * p.T_k);
 #pragma unroll
@@ -425,7 +428,9 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     p.wb = L.w[0];
     p.wr = L.w[1];
     const bool fp8 = p.elt == 1;
-    auto kern = fp8 ? indexer_tc_kernel<true> : indexer_tc_kernel<false>;
+    const bool flat = L.row_bstep != 0;
+    auto kern = fp8 ? (flat ? indexer_tc_kernel<true, true> : indexer_tc_kernel<true, false>)
+                    : (flat ? indexer_tc_kernel<false, true> : indexer_tc_kernel<false, false>);
     p.scores = scores;
     p.w = w;
     p.T_q = T_q;
