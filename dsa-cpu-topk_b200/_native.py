@@ -16,7 +16,9 @@ import os
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libdsa_b200.so")
+# DSA_LIB_VARIANT=checked loads the checked build (libdsa_b200_checked.so)
+LIB_PATH = os.path.join(HERE, "libdsa_b200_checked.so" if os.environ.get("DSA_LIB_VARIANT") == "checked"
+                        else "libdsa_b200.so")
 
 DSA_OK, DSA_ERR_INVALID, DSA_ERR_UNSUPPORTED, DSA_ERR_CUDA, DSA_ERR_TIMEOUT = 0, -1, -2, -3, -4
 DSA_F32, DSA_BF16, DSA_F16, DSA_FP8_E4M3 = 0, 1, 2, 3
@@ -92,6 +94,9 @@ def lib() -> ctypes.CDLL:
                                      i32, i32, lp, p, sz, p]
         L.dsa_quantize_fp8_rows.argtypes = [p, i32, i64, i64, i64, p, p, p]
         L.dsa_indexer_scores_fp8.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i64, i64, i32, lp, p]
+        L.dsa_debug_checks_enabled.restype = i32
+        L.dsa_debug_status.argtypes = [p]
+        L.dsa_debug_status.restype = i32
         L.dsa_forward_noalloc.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                           i64, i32, i32, p]
         for name in ("dsa_indexer_scores", "dsa_topk_select", "dsa_sparse_attn_threshold",
@@ -330,3 +335,8 @@ def indexer_scores_fp8(q8, k8, w, k_scale, scores, *, q_row0=0, row_bstep=0, fil
     _check(lib().dsa_indexer_scores_fp8(_ptr(q8), _ptr(k8), _ptr(w), _ptr(k_scale), _ptr(scores), B, T_q, T_k,
                                         q_row0, HI, DI, int(bool(fill_upper)), ctypes.byref(L), _stream()),
            "dsa_indexer_scores_fp8")
+
+
+def debug_status() -> int:
+    """Bits set by the checked build's failed index checks since the last call (0 normally)."""
+    return int(lib().dsa_debug_status(_stream()))

@@ -473,6 +473,7 @@ __device__ __forceinline__ Unit2 decode_unit2(int u, const AtParams& p) {
     r.qa = 2 * m;
     r.na = tile_blocks(r.qa, r.b, p);
     r.nb = r.qa + 1 < p.n_qt ? tile_blocks(r.qa + 1, r.b, p) : 0;
+    DSA_CHECK(r.b < p.B && r.qa < p.n_qt && r.na <= p.nkb, DBG_TILE);   // flagged only
     return r;
 }
 
@@ -1277,5 +1278,7 @@ int attn_tc(const uint32_t* bits, int64_t words, const void* Q, const void* K, c
     kern<<<grid, two ? NT2 : NTHREADS, smem, stream>>>(tmq, tmk, tmv, p);
     return check_launch(two ? "attn_tc2_kernel" : "attn_tc_kernel");
 }
+
+DSA_DEBUG_FLAGS_READER(attn_tc)
 
 }  // namespace dsa

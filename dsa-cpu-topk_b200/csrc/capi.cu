@@ -43,6 +43,14 @@ int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const f
                 int64_t T_q, int64_t T_k, int64_t q_row0, int64_t HQ, int64_t DQ, int64_t DV,
                 float scale, int dtype, const dsa_layout& L, cudaStream_t stream);
 
+unsigned debug_flags_sparse_attn();
+unsigned debug_flags_topk();
+unsigned debug_flags_attn_tc();
+unsigned debug_flags_indexer_tc();
+unsigned debug_flags_indexer_simt();
+unsigned debug_flags_fused_small();
+unsigned debug_flags_fp8_quant();
+
 namespace {
 thread_local std::string g_last_error;
 }
@@ -289,6 +297,23 @@ int dsa_device_status(void* stream) {
         return fail(DSA_ERR_TIMEOUT, "a tensor-core attention launch timed out waiting on its "
                                      "pipeline (its output is incomplete)");
     return DSA_OK;
+}
+
+int dsa_debug_checks_enabled(void) {
+#ifdef DSA_DEBUG_CHECKS
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+int dsa_debug_status(void* stream) {
+    clear_error();
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+        return fail(DSA_ERR_CUDA, "dsa_debug_status: stream synchronisation failed");
+    return (int)(debug_flags_sparse_attn() | debug_flags_topk() | debug_flags_attn_tc() |
+                 debug_flags_indexer_tc() | debug_flags_indexer_simt() | debug_flags_fused_small() |
+                 debug_flags_fp8_quant());
 }
 
 int64_t dsa_bitmap_words(int64_t T_k) { return T_k < 1 ? 0 : bitmap_words(T_k); }

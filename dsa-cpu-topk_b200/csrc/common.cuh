@@ -126,6 +126,39 @@ __device__ __forceinline__ float key2f(uint32_t k) {
     return __uint_as_float(b);
 }
 
+// ---- the checked build (-DDSA_DEBUG_CHECKS, libdsa_b200_checked.so) ----------
+// DSA_CHECK(cond, bit) is true in the normal build.  In the checked build a
+// false cond ORs `bit` into this file's device flag word instead of letting
+// the guarded access happen (the caller skips it); dsa_debug_status() reads
+// and clears every file's word.  No trap, no fault.
+enum DebugBit : unsigned {
+    DBG_LIST_KEY = 1u,      // a kept-index list entry outside 0 <= s <= t (stage 3 list form)
+    DBG_CAND_OVERFLOW = 2u, // a top-K candidate past the candidate buffer
+    DBG_TILE = 4u,          // a decoded tile / unit outside the launch's shape
+    DBG_WORD = 8u,          // a bitmap word past the row's words
+};
+#ifdef DSA_DEBUG_CHECKS
+static __device__ unsigned int g_dsa_debug_flags;   // one word per .cu file (no relocatable device code)
+__device__ __forceinline__ bool dsa_check_fail(unsigned bit) {
+    atomicOr(&g_dsa_debug_flags, bit);
+    return false;
+}
+#define DSA_CHECK(cond, bit) ((cond) ? true : ::dsa::dsa_check_fail(bit))
+// host: read and clear this file's flag word (0 on error)
+static inline unsigned take_debug_flags_here() {
+    unsigned f = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&f, g_dsa_debug_flags, sizeof f) != cudaSuccess) return 0;
+    if (f) cudaMemcpyToSymbol(g_dsa_debug_flags, &z, sizeof z);
+    return f;
+}
+#else
+#define DSA_CHECK(cond, bit) true
+static inline unsigned take_debug_flags_here() { return 0; }
+#endif
+// Each kernel file exports its flag reader under its own name.
+#define DSA_DEBUG_FLAGS_READER(name) \
+    unsigned debug_flags_##name() { return take_debug_flags_here(); }
+
 __device__ __forceinline__ uint4 ldg16(const void* p) {
     return __ldg(reinterpret_cast<const uint4*>(p));
 }

@@ -41,6 +41,8 @@ int launch_q(const void* x, int64_t rows, int64_t D, int64_t stride, void* out, 
 }
 
 }  // namespace
+DSA_DEBUG_FLAGS_READER(fp8_quant)
+
 }  // namespace dsa
 
 using namespace dsa;

@@ -373,4 +373,6 @@ int fused_small_forward(const void* q_idx, const void* k_idx, const float* w_idx
 #undef DSA_FS
 }
 
+DSA_DEBUG_FLAGS_READER(fused_small)
+
 }  // namespace dsa

@@ -320,4 +320,6 @@ int indexer_scores_simt(const void* q, const void* k, const float* w, float* sco
     }
 }
 
+DSA_DEBUG_FLAGS_READER(indexer_simt)
+
 }  // namespace dsa

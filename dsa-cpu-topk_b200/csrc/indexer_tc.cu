@@ -100,6 +100,7 @@ __device__ __forceinline__ void decode_tile(int lin, const int* pref, const TcPa
         i = lo;
         j = r - pref[lo];
     }
+    DSA_CHECK(b < p.B && i < p.n_tblk && j < p.nsb, DBG_TILE);   // flagged only: the walk stays as it is
 }
 
 template <bool FP8, bool FLAT>
@@ -545,5 +546,7 @@ int indexer_scores_tc(const void* q, const void* k, const float* w, float* score
     kern<<<grid, NTHREADS, smem, stream>>>(tmq, tmk, tms, p);
     return check_launch("indexer_tc_kernel");
 }
+
+DSA_DEBUG_FLAGS_READER(indexer_tc)
 
 }  // namespace dsa

@@ -167,7 +167,10 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
         int n;
         if (list_mode) {
             n = (int)(n_total - c0 < LIST ? n_total - c0 : LIST);
-            for (int i = tid; i < n; i += BLOCK) keys_s[i] = __ldg(a.idx + row * a.idx_cap + c0 + i);
+            for (int i = tid; i < n; i += BLOCK) {
+                const int32_t key = __ldg(a.idx + row * a.idx_cap + c0 + i);
+                keys_s[i] = DSA_CHECK(key >= 0 && key < valid, DBG_LIST_KEY) ? key : -1;
+            }
             __syncthreads();
         } else {
             const int64_t s = c0 + tid;
@@ -194,6 +197,9 @@ __global__ void __launch_bounds__(BLOCK, MINB) sparse_attn_kernel(AttnArgs<T> a)
             for (int u = 0; u < U; ++u) {
                 const int j = base + team + u * P;
                 ok[u] = active && j < n;
+#ifdef DSA_DEBUG_CHECKS
+                ok[u] = ok[u] && keys_s[j] >= 0;   // an entry the check dropped
+#endif
                 const int64_t key = ok[u] ? (int64_t)keys_s[j] : 0;
 #pragma unroll
                 for (int c = 0; c < C; ++c) {
@@ -352,6 +358,7 @@ __global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
         if (list_mode) {
             n = (int)(n_total - c0 < 32 ? n_total - c0 : 32);
             if (lane < n) mykey = __ldg(a.idx + row * a.idx_cap + c0 + lane);
+            if (lane < n && !DSA_CHECK(mykey >= 0 && mykey < valid, DBG_LIST_KEY)) mykey = -1;
         } else {
             const int64_t s = c0 + lane;
             const uint32_t bal = __ballot_sync(0xffffffffu, s < n_total && __ldg(srow + s) >= thr);
@@ -366,6 +373,9 @@ __global__ void __launch_bounds__(256) sparse_attn_warp_kernel(AttnArgs<T> a) {
                 const int j = base + team + u * P;
                 ok[u] = j < n;
                 const int s = __shfl_sync(0xffffffffu, mykey, j & 31);
+#ifdef DSA_DEBUG_CHECKS
+                ok[u] = ok[u] && s >= 0;   // an entry the check dropped
+#endif
                 const int64_t key = ok[u] ? s : 0;
 #pragma unroll
                 for (int c = 0; c < C; ++c) {
@@ -550,5 +560,7 @@ int sparse_attn(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const f
     }
 #undef DSA_ATTN_ARGS
 }
+
+DSA_DEBUG_FLAGS_READER(sparse_attn)
 
 }  // namespace dsa

@@ -682,8 +682,10 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                         for (int j = 0; j < 4; ++j)
                             if (e[j] - lo < (1u << S0) && (g + 1 < g4 || 4 * g + j < valid)) {
                                 const uint32_t at = atomicAdd(&n_cand, 1u);
-                                cand_key[at] = e[j];
-                                cand_pos[at] = 4 * g + j;
+                                if (DSA_CHECK(at < (uint32_t)a.cand_max, DBG_CAND_OVERFLOW)) {
+                                    cand_key[at] = e[j];
+                                    cand_pos[at] = 4 * g + j;
+                                }
                             }
                     }
                 }
@@ -711,8 +713,10 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
                     while (m) {
                         const int pos = w * 32 + __ffs(m) - 1;
                         m &= m - 1;
-                        cand_key[at] = f2key_raw(__ldg(src + pos));   // no NaN on this path
-                        cand_pos[at] = pos;
+                        if (DSA_CHECK(at < (uint32_t)a.cand_max, DBG_CAND_OVERFLOW)) {
+                            cand_key[at] = f2key_raw(__ldg(src + pos));   // no NaN on this path
+                            cand_pos[at] = pos;
+                        }
                         ++at;
                     }
                 }
@@ -783,8 +787,10 @@ __global__ void __launch_bounds__(BLOCK, CACHED ? 1 : 1280 / BLOCK) topk_cached_
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         if ((e[j] >> S0) == d0) {
-                            cand_key[base] = e[j];
-                            cand_pos[base] = 4 * g + j;
+                            if (DSA_CHECK(base < (uint32_t)a.cand_max, DBG_CAND_OVERFLOW)) {
+                                cand_key[base] = e[j];
+                                cand_pos[base] = 4 * g + j;
+                            }
                             ++base;
                         }
                 }
@@ -1399,5 +1405,7 @@ static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream) {
     if (longest <= 16384) return launch_topk<512>(a, stream);
     return launch_topk<1024>(a, stream);
 }
+
+DSA_DEBUG_FLAGS_READER(topk)
 
 }  // namespace dsa

@@ -120,6 +120,22 @@ DSA_API const char* dsa_last_error_string(void);
 DSA_API int dsa_device_status(void* stream);
 
 /*
+ * Checked build.  libdsa_b200_checked.so is this library compiled with
+ * -DDSA_DEBUG_CHECKS (`python dsa-cpu-topk_b200/build.py --checked`): every
+ * guarded access checks its index first, and a failing check sets a bit in a
+ * device flag word instead of performing the access (no trap, no fault):
+ *   1  a kept-index list entry outside 0 <= s <= t (dsa_sparse_attn): skipped
+ *   2  a top-K candidate past the candidate buffer: not stored
+ *   4  a decoded indexer tile or attention unit outside the launch's shape
+ * dsa_debug_status synchronises `stream`, then returns the OR of the bits set
+ * since the last call and clears them (always 0 in the normal build);
+ * dsa_debug_checks_enabled says which build is loaded.  No counterpart in the
+ * reference, which validates on the host only (topk_avx512.cpp:227-235).
+ */
+DSA_API int dsa_debug_checks_enabled(void);
+DSA_API int dsa_debug_status(void* stream);
+
+/*
  * Stage 1 — Lightning Indexer scores.
  *   q       [B, T_q, HI, DI]  dtype      indexer queries of rows q_row0..q_row0+T_q-1
  *   k       [B, T_k, DI]      dtype      shared indexer key

@@ -91,3 +91,13 @@ def test_bitmap_entry_points_validate_on_the_host(lib):
     rc = lib.dsa_sparse_attn_bitmap(None, 32, fake, fake, fake, fake, 1, 128, 1024, 0, 4, 128, 128,
                                     ctypes.c_float(0.1), _native.DSA_BF16, None)
     assert rc == _native.DSA_ERR_INVALID
+
+
+def test_checked_library_exports_every_declared_symbol():
+    """libdsa_b200_checked.so (index checks that flag instead of faulting) has the same boundary."""
+    import build
+    path = build.build(checked=True)
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (dsa_\w+)", out))
+    missing = [n for n in declared() if n not in exported]
+    assert not missing, missing
