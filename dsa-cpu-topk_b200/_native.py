@@ -71,6 +71,9 @@ def lib() -> ctypes.CDLL:
         L.dsa_topk_select_bitmap.argtypes = [p, i64, i64, i64, i64, i32, i64, p, p, p, i64, p]
         L.dsa_sparse_attn_bitmap.argtypes = [p, i64, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
                                              f32, i32, p]
+        L.dsa_topk_select_bitmap_workspace_bytes.argtypes = [i64, i64]
+        L.dsa_topk_select_bitmap_workspace_bytes.restype = sz
+        L.dsa_topk_select_bitmap_ws.argtypes = [p, i64, i64, i64, i64, i32, i64, p, p, p, i64, p, sz, p]
         L.dsa_device_status.argtypes = [p]
         L.dsa_device_status.restype = i32
         L.dsa_forward_workspace_bytes.argtypes = [i64, i64, i64, i64]
@@ -103,7 +106,8 @@ def lib() -> ctypes.CDLL:
                      "dsa_sparse_attn", "dsa_forward", "dsa_kept_bitmap", "dsa_sparse_attn_bitmap",
                      "dsa_topk_select_bitmap", "dsa_indexer_scores_ex", "dsa_topk_select_ex",
                      "dsa_sparse_attn_ex", "dsa_sparse_attn_bitmap_ex", "dsa_forward_ex",
-                     "dsa_forward_noalloc", "dsa_quantize_fp8_rows", "dsa_indexer_scores_fp8"):
+                     "dsa_forward_noalloc", "dsa_quantize_fp8_rows", "dsa_indexer_scores_fp8",
+                     "dsa_topk_select_bitmap_ws"):
             getattr(L, name).restype = i32
         _lib = L
     return _lib
@@ -207,12 +211,25 @@ def kept_bitmap(scores, thr, bits, *, q_row0=0):
                                  bits.shape[-1], _stream()), "dsa_kept_bitmap")
 
 
-def topk_select_bitmap(scores, k, thr, bits, cnt=None, *, causal=True, q_row0=0):
-    """Threshold (+ count) and kept-set bitmap of every row of scores [B, T_q, T_k]."""
+def topk_select_bitmap_workspace_bytes(n_rows, words):
+    return int(lib().dsa_topk_select_bitmap_workspace_bytes(n_rows, words))
+
+
+def topk_select_bitmap(scores, k, thr, bits, cnt=None, *, causal=True, q_row0=0, workspace=None):
+    """Threshold (+ count) and kept-set bitmap of every row of scores [B, T_q, T_k].
+
+    With a workspace (uint8 CUDA tensor of topk_select_bitmap_workspace_bytes)
+    rows of 4K-32K entries take the sweep + resolve kernels."""
     B, T_q, T_k = scores.shape
-    _check(lib().dsa_topk_select_bitmap(_ptr(scores), B * T_q, T_k, T_q, q_row0, int(bool(causal)), k,
-                                        _ptr(thr), _ptr(cnt), _ptr(bits), bits.shape[-1], _stream()),
-           "dsa_topk_select_bitmap")
+    if workspace is None:
+        _check(lib().dsa_topk_select_bitmap(_ptr(scores), B * T_q, T_k, T_q, q_row0, int(bool(causal)), k,
+                                            _ptr(thr), _ptr(cnt), _ptr(bits), bits.shape[-1], _stream()),
+               "dsa_topk_select_bitmap")
+        return
+    _check(lib().dsa_topk_select_bitmap_ws(_ptr(scores), B * T_q, T_k, T_q, q_row0, int(bool(causal)), k,
+                                           _ptr(thr), _ptr(cnt), _ptr(bits), bits.shape[-1], _ptr(workspace),
+                                           workspace.numel(), _stream()),
+           "dsa_topk_select_bitmap_ws")
 
 
 def sparse_attn_bitmap(bits, Q, K, V, O, *, q_row0=0, scale=None):

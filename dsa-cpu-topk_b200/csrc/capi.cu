@@ -24,7 +24,8 @@ int indexer_tc_take_timeout(cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
                 int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
                 int32_t* idx, int32_t* cnt, int64_t idx_cap, uint32_t* bits, int64_t words,
-                int64_t row_bstep, cudaStream_t stream);
+                int64_t row_bstep, cudaStream_t stream, void* ws = nullptr, size_t ws_bytes = 0);
+size_t topk_sweep_ws_bytes(int64_t n_rows, int64_t words);
 int fused_small_forward(const void* q_idx, const void* k_idx, const float* w_idx, const void* Q,
                         const void* K, const void* V, float* O, int64_t B, int64_t T_q, int64_t T_k,
                         int64_t q_row0, int64_t HI, int64_t DI, int64_t HQ, int64_t DQ, int64_t DV,
@@ -116,8 +117,11 @@ static ForwardLayout forward_layout(int64_t B, int64_t T_q, int64_t T_k, int64_t
     L.cnt = off;
     off += align256((size_t)rows * sizeof(int32_t));
     L.idx = off;
-    off += align256((size_t)rows * (size_t)L.idx_cap * sizeof(int32_t));
     L.words = bitmap_words(T_k);
+    // the index lists (gather path), or the bitmap top-K's candidate words (tensor-core path)
+    const size_t list_bytes = (size_t)rows * (size_t)L.idx_cap * sizeof(int32_t);
+    const size_t cand_bytes = topk_sweep_ws_bytes(rows, L.words);
+    off += align256(list_bytes > cand_bytes ? list_bytes : cand_bytes);
     L.bits = off;
     off += align256((size_t)rows * (size_t)L.words * sizeof(uint32_t));
     L.total = off;
@@ -251,6 +255,26 @@ int dsa_topk_select_bitmap(const float* scores, int64_t n_rows, int64_t row_len,
     if (!bits) return fail(DSA_ERR_INVALID, "topk_select_bitmap: bits is required");
     return dsa_topk_select_ex(scores, n_rows, row_len, row_len, rows_per_batch, q_row0, 0, causal, k,
                               thr_out, nullptr, cnt_out, 0, bits, words_per_row, stream);
+}
+
+size_t dsa_topk_select_bitmap_workspace_bytes(int64_t n_rows, int64_t words_per_row) {
+    if (n_rows < 0 || words_per_row < 1) return 0;
+    return topk_sweep_ws_bytes(n_rows, words_per_row);
+}
+
+int dsa_topk_select_bitmap_ws(const float* scores, int64_t n_rows, int64_t row_len,
+                              int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
+                              float* thr_out, int32_t* cnt_out, uint32_t* bits, int64_t words_per_row,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (!bits) return fail(DSA_ERR_INVALID, "topk_select_bitmap: bits is required");
+    if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(DSA_ERR_INVALID, "topk_select_bitmap: workspace must be 256-byte aligned");
+    if (n_rows > 0 && workspace_bytes < dsa_topk_select_bitmap_workspace_bytes(n_rows, words_per_row))
+        return fail(DSA_ERR_INVALID, "topk_select_bitmap: workspace too small");
+    return topk_select(scores, n_rows, row_len, row_len, rows_per_batch, q_row0, causal, k, thr_out,
+                       nullptr, cnt_out, 0, bits, words_per_row, 0, (cudaStream_t)stream, workspace,
+                       workspace_bytes);
 }
 
 int dsa_sparse_attn_ex(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const float* scores,
@@ -424,7 +448,7 @@ int dsa_forward_ex(const void* q_idx, const void* k_idx, const float* w_idx, con
         // threshold and kept-set bitmap, then tensor-core attention
         uint32_t* bits = reinterpret_cast<uint32_t*>(ws + W.bits);
         rc = topk_select(scores, B * T_q, T_k, T_k, T_q, q_row0, /*causal=*/1, k, thr, nullptr,
-                         nullptr, 0, bits, W.words, L.row_bstep, st);
+                         nullptr, 0, bits, W.words, L.row_bstep, st, ws + W.idx, W.bits - W.idx);
         if (rc) return rc;
         // stage 3's workspace (block summary; fp16 copy of V for bf16 inputs):
         // over the dead score and list region, else after the workspace; with

@@ -20,6 +20,10 @@
 //               candidates; list rows emit ascending positions by
 //               warp-segmented ballots.  Rows up to 8K with lists cache the keys
 //               in shared memory; the others re-read the row from L2.
+//               Bitmap-only rows given a workspace (the forward's) take
+//               topk_sweep_kernel + topk_resolve_kernel instead: a 12-bit
+//               first digit, two sweeps with four block barriers per row,
+//               and the bin-d0 candidates resolved one warp per row.
 //   > 32K       topk_select_kernel: four 8-bit passes, each filtering the row
 // Rows with fewer causal entries than k keep every causal entry (threshold
 // -inf).  Output is deterministic: lists are in ascending position order.
@@ -929,6 +933,422 @@ int launch_cached(TopkArgs a, int64_t longest, cudaStream_t stream, int cand_div
 }
 
 // ===========================================================================
+// Bitmap-only rows of 4K..32K entries (the forward's c4 and c5 rows) in two
+// kernels, given a workspace.  The first streams the rows with four block
+// barriers per row; the second resolves each row's threshold from its
+// candidates, one warp per row.
+//
+// topk_sweep_kernel, one CTA per row:
+//   sweep 1 (HBM)  histogram of the keys' top DBITS bits (12: sign, exponent
+//                  and three mantissa bits, so the bin holding the k-th
+//                  largest key of a c5 row keeps a few hundred keys)
+//   find           the bin d0 holding the k-th largest key and the rank krem
+//                  left inside it; each thread zeroes the bins it scanned, so
+//                  the histogram is clear for the next row without a pass
+//   sweep 2 (L2)   per 32 positions, one ballot gives the word of keys above
+//                  bin d0 (final bits of the bitmap), one the word of keys in
+//                  bin d0; after each 1024-position chunk the warp appends
+//                  that chunk's bin-d0 keys and positions to the row's
+//                  candidate list (one shared add per chunk; the keys are read
+//                  back while the chunk is still in L2)
+//   The row's (d0, krem, count) go to a meta word; the row ends without a
+//   barrier, so warps run ahead into the next row's sweep 1.  Rows shorter
+//   than k, rows holding NaN or an infinity (keys in the 16 edge bins at
+//   either end) and rows whose bin d0 holds more keys than the list are
+//   finished here (short_row_block / exact_row_slow) and marked done.
+// topk_resolve_kernel, one warp per row:
+//   three radix passes (8 + 8 + 4 bits) over the candidates' low 20 bits for
+//   the exact krem-th largest, the kept candidates ORed into the bitmap, the
+//   row's threshold and count.
+// Output equals the one-kernel path's: threshold, count, bitmap words.
+// ===========================================================================
+constexpr uint32_t kRowDone = 0xffffffffu;   // meta.x of a row finished by the sweep kernel
+
+template <int BLOCK, int DBITS>
+__device__ __forceinline__ void fine_find(uint32_t* hist, uint32_t krem, uint32_t* wtot,
+                                          uint32_t* res) {
+    constexpr int NB = 1 << DBITS;
+    constexpr int PER4 = NB / (4 * BLOCK);   // uint4 slots per thread
+    static_assert(PER4 >= 1, "fine_find: at least 4 bins per thread");
+    uint4* h4 = reinterpret_cast<uint4*>(hist) + threadIdx.x * PER4;
+    uint32_t local = 0;
+#pragma unroll
+    for (int i = 0; i < PER4; ++i) {
+        const uint4 v = h4[i];
+        local += v.x + v.y + v.z + v.w;
+    }
+    // the edge bins (slots 0-15: NaN/+inf; slots NB-16..NB-1: -inf/-NaN)
+    if (threadIdx.x == 0 || threadIdx.x == BLOCK - 1) {
+        uint32_t e = 0;
+        const int s0 = threadIdx.x == 0 ? 0 : NB - 16;
+        for (int i = 0; i < 16; ++i) e |= hist[s0 + i];
+        res[threadIdx.x == 0 ? 3 : 4] = e;
+    }
+    uint32_t tot;
+    const uint32_t excl = block_excl_scan<BLOCK>(local, wtot, &tot);
+    if (excl < krem && krem <= excl + local) {
+        uint32_t c = excl;
+        const int r0 = threadIdx.x * PER4 * 4;
+        for (int i = 0; i < PER4 * 4; ++i) {
+            const uint32_t h = hist[r0 + i];
+            if (krem <= c + h) {
+                res[0] = (uint32_t)(NB - 1 - (r0 + i));
+                res[1] = krem - c;
+                res[2] = h;
+                break;
+            }
+            c += h;
+        }
+    }
+    // every thread clears the slots it scanned (the crossing thread after its re-read)
+#pragma unroll
+    for (int i = 0; i < PER4; ++i) h4[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+}
+
+// Candidate lists of the two-kernel bitmap path: per row, cap keys and cap
+// 16-bit positions (rows of up to 32768 positions), and a meta word.
+struct CandLists {
+    uint32_t* key;   // [n_rows][cap]
+    uint16_t* pos;   // [n_rows][cap]
+    uint4* meta;     // [n_rows]: d0 (kRowDone: row finished by the sweep), krem, candidate count
+    int cap;
+};
+
+// candidates a row may hold: 1/16 of its positions, 256..1024
+__host__ __device__ inline int cand_cap_for(int64_t words) {
+    const int64_t c = words * 2;
+    return (int)(c < 256 ? 256 : c > 1024 ? 1024 : c);
+}
+
+inline size_t align256_sz(size_t x) { return (x + 255) / 256 * 256; }
+
+size_t sweep_ws_bytes(int64_t n_rows, int64_t words) {
+    const size_t cap = (size_t)cand_cap_for(words);
+    return align256_sz((size_t)n_rows * cap * sizeof(uint32_t)) + align256_sz((size_t)n_rows * cap * sizeof(uint16_t)) +
+           (size_t)n_rows * sizeof(uint4);
+}
+
+CandLists cand_lists(void* ws, int64_t n_rows, int64_t words) {
+    CandLists c;
+    c.cap = cand_cap_for(words);
+    char* p = static_cast<char*>(ws);
+    c.key = reinterpret_cast<uint32_t*>(p);
+    p += align256_sz((size_t)n_rows * c.cap * sizeof(uint32_t));
+    c.pos = reinterpret_cast<uint16_t*>(p);
+    p += align256_sz((size_t)n_rows * c.cap * sizeof(uint16_t));
+    c.meta = reinterpret_cast<uint4*>(p);
+    return c;
+}
+
+// Sweep 2 over one chunk of 32 words (1024 positions) of a row: lane L reads
+// position 32*i + L of word i, so one ballot gives word i's kept bits (keys
+// above bin d0) and another its candidates (keys inside bin d0); lane 0
+// stages both words in the warp's shared words.  CHECK: the chunk reaches
+// past the row's causal end.
+template <bool CHECK, int SW>
+__device__ __forceinline__ void sweep2_chunk(const float* p, int left, float lo_f, float hi_f, int lane,
+                                             uint32_t* st_ab, uint32_t* st_cb) {
+#pragma unroll
+    for (int i0 = 0; i0 < 32; i0 += SW) {
+        float x[SW];
+#pragma unroll
+        for (int u = 0; u < SW; ++u) {
+            const int o = (i0 + u) * 32;
+            if (CHECK)
+                x[u] = o + lane < left ? __ldg(p + o) : __uint_as_float(0xff800000u);
+            else
+                x[u] = __ldg(p + o);
+        }
+#pragma unroll
+        for (int u = 0; u < SW; ++u) {
+            const uint32_t ab = __ballot_sync(0xffffffffu, x[u] >= hi_f);
+            const uint32_t ge = __ballot_sync(0xffffffffu, x[u] >= lo_f);
+            if (lane == 0) {
+                st_ab[i0 + u] = ab;
+                st_cb[i0 + u] = ge & ~ab;
+            }
+        }
+    }
+}
+
+// slot of a score in the descending first-digit histogram: (~key) >> S, where
+// key is the order-preserving key of x (x + 0 turns -0 into +0)
+template <int S>
+__device__ __forceinline__ uint32_t desc_slot(float x) {
+    const uint32_t b = __float_as_uint(x + 0.0f);
+    const uint32_t s = (uint32_t)((int32_t)b >> 31);
+    return (b ^ (~s & 0x7fffffffu)) >> S;
+}
+
+template <int BLOCK, int DBITS, int PIPE, int MINB, int SW2>
+__global__ void __launch_bounds__(BLOCK, MINB) topk_sweep_kernel(TopkArgs a, CandLists cl) {
+    constexpr int NW = BLOCK / 32;
+    constexpr int NB = 1 << DBITS;
+    constexpr int S = 32 - DBITS;   // shift of the first digit
+    __shared__ __align__(16) uint32_t hist[NB];
+    __shared__ uint32_t stage[NW][2][32];
+    __shared__ uint32_t wtot[NW];
+    __shared__ uint32_t res[5];
+    __shared__ uint32_t s_cnt;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    for (int i = tid; i < NB; i += BLOCK) hist[i] = 0;
+    __syncthreads();
+
+    for (int64_t row = blockIdx.x; row < a.n_rows; row += gridDim.x) {
+        const float* src = a.scores + row * a.row_stride;
+        const int valid = (int)row_valid(a, row);
+        uint32_t* out = a.bits + row * a.words;
+        if (a.k > valid) {
+            short_row_block<BLOCK>(a, row, src, valid, wtot);
+            if (tid == 0) cl.meta[row] = make_uint4(kRowDone, 0u, 0u, 0u);
+            continue;   // block-uniform
+        }
+        // ---- sweep 1: first-digit histogram
+        const int gfull = a.vec_ok ? valid >> 2 : 0;   // whole float4 groups read as vectors
+        {
+            const float4* p4 = reinterpret_cast<const float4*>(src) + tid;
+            int g = tid;
+            for (; g + (PIPE - 1) * BLOCK < gfull; g += PIPE * BLOCK, p4 += PIPE * BLOCK) {
+                float4 v[PIPE];
+#pragma unroll
+                for (int u = 0; u < PIPE; ++u) v[u] = __ldg(p4 + u * BLOCK);
+#pragma unroll
+                for (int u = 0; u < PIPE; ++u) {
+                    atomicAdd(&hist[desc_slot<S>(v[u].x)], 1u);
+                    atomicAdd(&hist[desc_slot<S>(v[u].y)], 1u);
+                    atomicAdd(&hist[desc_slot<S>(v[u].z)], 1u);
+                    atomicAdd(&hist[desc_slot<S>(v[u].w)], 1u);
+                }
+            }
+            for (; g < gfull; g += BLOCK, p4 += BLOCK) {
+                const float4 v = __ldg(p4);
+                atomicAdd(&hist[desc_slot<S>(v.x)], 1u);
+                atomicAdd(&hist[desc_slot<S>(v.y)], 1u);
+                atomicAdd(&hist[desc_slot<S>(v.z)], 1u);
+                atomicAdd(&hist[desc_slot<S>(v.w)], 1u);
+            }
+            for (int i = 4 * gfull + tid; i < valid; i += BLOCK) atomicAdd(&hist[desc_slot<S>(__ldg(src + i))], 1u);
+        }
+        __syncthreads();
+        // every warp's appends of the previous row precede the barrier above,
+        // and this row's follow the one that ends fine_find
+        if (tid == 0) s_cnt = 0;
+        fine_find<BLOCK, DBITS>(hist, (uint32_t)a.k, wtot, res);
+        const uint32_t d0 = res[0], krem = res[1], n0 = res[2];
+        const bool plain = (res[3] | res[4]) == 0u;
+        if (!plain || n0 > (uint32_t)cl.cap) {   // block-uniform
+            exact_row_slow<BLOCK>(src, valid, a.k, a.thr + row, a.cnt ? a.cnt + row : nullptr, nullptr, 0,
+                                  out, a.words, hist, wtot, res);
+            for (int i = tid; i < 256; i += BLOCK) hist[i] = 0;
+            if (tid == 0) cl.meta[row] = make_uint4(kRowDone, 0u, 0u, 0u);
+            __syncthreads();
+            continue;
+        }
+        // ---- sweep 2: plain rows have every key in bins 16..NB-17, so both
+        // edges of bin d0 are finite (hi may be +inf for the top finite bin);
+        // exactly n0 keys lie in bin d0, so the appends fit the list
+        const float hi_f = key2f((d0 + 1) << S), lo_f = key2f(d0 << S);
+        uint32_t* ckey = cl.key + row * cl.cap;
+        uint16_t* cpos = cl.pos + row * cl.cap;
+        uint32_t* st_ab = stage[warp][0];
+        uint32_t* st_cb = stage[warp][1];
+        const int nwords = (int)a.words;
+        for (int ch = warp; ch < ((nwords + 31) >> 5); ch += NW) {
+            const int s0c = ch * 1024;
+            const float* p = src + s0c + lane;
+            const int wd = ch * 32 + lane;
+            if (s0c >= valid) {   // words past the causal end
+                if (wd < nwords) out[wd] = 0u;
+                continue;
+            }
+            if (s0c + 1024 <= valid)
+                sweep2_chunk<false, SW2>(p, valid - s0c, lo_f, hi_f, lane, st_ab, st_cb);
+            else
+                sweep2_chunk<true, SW2>(p, valid - s0c, lo_f, hi_f, lane, st_ab, st_cb);
+            __syncwarp();
+            if (wd < nwords) out[wd] = st_ab[lane];
+            // the chunk's candidates: lane L takes word L's set bits, reserves
+            // their slots with one shared add per chunk, and reads their keys
+            // back (the chunk was just read, so from L2), four at a time
+            uint32_t m = st_cb[lane];
+            const uint32_t c = __popc(m);
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
+            if (tot) {   // warp-uniform
+                uint32_t base = 0;
+                if (lane == 0) base = atomicAdd(&s_cnt, tot);
+                uint32_t at = __shfl_sync(0xffffffffu, base, 0) + incl - c;
+                const int pw = s0c + lane * 32;
+                while (m) {
+                    int ps[4];
+                    float v[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        ps[j] = m ? pw + __ffs(m) - 1 : -1;
+                        m &= m - 1;
+                        v[j] = ps[j] >= 0 ? __ldg(src + ps[j]) : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (ps[j] >= 0) {
+                            ckey[at] = f2key_raw(v[j]);
+                            cpos[at] = (uint16_t)ps[j];
+                            ++at;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        if (tid == 0) cl.meta[row] = make_uint4(d0, krem, n0, 0u);
+    }
+}
+
+// One warp per row: the exact krem-th largest key among the row's bin-d0
+// candidates (read from the row's list), their bits ORed into the bitmap,
+// the threshold and the count.  Per warp in shared memory: cap keys and a
+// 256-bin histogram.
+template <int DBITS>
+__global__ void __launch_bounds__(256, 4) topk_resolve_kernel(TopkArgs a, CandLists cl) {
+    constexpr int S = 32 - DBITS;
+    extern __shared__ uint4 dyn_r[];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    uint32_t* key = reinterpret_cast<uint32_t*>(dyn_r) + (size_t)wib * (cl.cap + 256);
+    uint32_t* hist = key + cl.cap;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + wib; row < a.n_rows; row += nwarps) {
+        const uint4 m = cl.meta[row];
+        if (m.x == kRowDone) continue;   // warp-uniform
+        const uint32_t d0 = m.x;
+        uint32_t krem = m.y;
+        const uint32_t n = m.z <= (uint32_t)cl.cap ? m.z : (uint32_t)cl.cap;
+        const uint32_t above = (uint32_t)a.k - krem;
+        const uint32_t* ckey = cl.key + row * cl.cap;
+        const uint16_t* cpos = cl.pos + row * cl.cap;
+        uint32_t* out = a.bits + row * a.words;
+        for (uint32_t i0 = 0; i0 < n; i0 += 256) {
+            uint32_t x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t i = i0 + u * 32 + lane;
+                x[u] = i < n ? ckey[i] : 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t i = i0 + u * 32 + lane;
+                if (i < n) key[i] = x[u];
+            }
+        }
+        // radix passes over the remaining S bits: 8, 8, then the rest
+        uint32_t prefix = d0 << S, pmask = ~0u << S;
+#pragma unroll 1
+        for (int left = S; left > 0;) {
+            const int nbits = left > 8 ? 8 : left;
+            const int shift = left - nbits;
+            const uint32_t nb = 1u << nbits;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) hist[lane + 32 * j] = 0;
+            __syncwarp();
+            for (uint32_t i = lane; i < n; i += 32) {
+                const uint32_t kk = key[i];
+                if ((kk & pmask) == prefix) atomicAdd(&hist[(nb - 1) - ((kk >> shift) & (nb - 1))], 1u);
+            }
+            __syncwarp();
+            // lane L scans slots [8L, 8L+8) (descending digits)
+            uint32_t h[8], local = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                h[j] = hist[8 * lane + j];
+                local += h[j];
+            }
+            uint32_t inc = local;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += y;
+            }
+            const uint32_t excl = inc - local;
+            uint32_t dsel = 0, rsel = 0;
+            const bool mine = excl < krem && krem <= inc;
+            if (mine) {
+                uint32_t cc = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (rsel == 0 && krem <= cc + h[j]) {
+                        dsel = (nb - 1) - (uint32_t)(8 * lane + j);
+                        rsel = krem - cc;
+                    }
+                    cc += h[j];
+                }
+            }
+            const int src_lane = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+            dsel = __shfl_sync(0xffffffffu, dsel, src_lane);
+            rsel = __shfl_sync(0xffffffffu, rsel, src_lane);
+            prefix |= dsel << shift;
+            pmask |= (nb - 1) << shift;
+            krem = rsel;
+            left -= nbits;
+            __syncwarp();
+        }
+        // kept candidates: their bits, and the count
+        uint32_t kc = 0;
+        for (uint32_t i = lane; i < n; i += 32) {
+            if (key[i] >= prefix) {
+                const uint32_t ps = cpos[i];
+                atomicOr(out + (ps >> 5), 1u << (ps & 31));
+                ++kc;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) kc += __shfl_xor_sync(0xffffffffu, kc, o);
+        if (lane == 0) {
+            a.thr[row] = key2f(prefix);
+            if (a.cnt) a.cnt[row] = (int32_t)(above + kc);
+        }
+        __syncwarp();
+    }
+}
+
+constexpr int kSweepDBits = 12;
+
+int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
+    const CandLists cl = cand_lists(ws, a.n_rows, a.words);
+    {
+        constexpr int BLOCK = 256;
+        // 6 CTAs of 256 threads per SM (40 registers; more CTAs spill, fewer measured slower)
+        auto kern = topk_sweep_kernel<BLOCK, kSweepDBits, 4, 6, 4>;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, BLOCK, 0) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        int64_t grid = (int64_t)num_sms() * per_sm;
+        if (grid > a.n_rows) grid = a.n_rows;
+        kern<<<(unsigned)grid, BLOCK, 0, stream>>>(a, cl);
+        if (int rc = check_launch("topk_sweep_kernel")) return rc;
+    }
+    {
+        auto kern = topk_resolve_kernel<kSweepDBits>;
+        const size_t smem = 8 * ((size_t)cl.cap + 256) * sizeof(uint32_t);
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return fail(DSA_ERR_CUDA, "topk_resolve: cannot set dynamic shared memory size");
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        int64_t grid = (int64_t)num_sms() * per_sm;
+        const int64_t need = (a.n_rows + 7) / 8;
+        if (grid > need) grid = need;
+        kern<<<(unsigned)grid, 256, smem, stream>>>(a, cl);
+        return check_launch("topk_resolve_kernel");
+    }
+}
+
+// ===========================================================================
 // Short rows (<= 512 entries: configs c1 and c3): one warp
 // per row, the row's keys in registers (NG float4 groups per lane), no block
 // barriers.  Four 8-bit radix passes over the register-resident keys use a
@@ -1308,6 +1728,9 @@ int launch_warp_l2(const TopkArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
+// Workspace of the two-kernel bitmap path (candidate words, one meta word per row).
+size_t topk_sweep_ws_bytes(int64_t n_rows, int64_t words) { return sweep_ws_bytes(n_rows, words); }
+
 int kept_bitmap(const float* scores, const float* thr, uint32_t* bits, int64_t B, int64_t T_q,
                 int64_t T_k, int64_t q_row0, int64_t words, int64_t row_bstep, cudaStream_t stream);
 int64_t bitmap_words(int64_t T_k);
@@ -1317,7 +1740,7 @@ static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream);
 int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t row_stride,
                 int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k, float* thr,
                 int32_t* idx, int32_t* cnt, int64_t idx_cap, uint32_t* bits, int64_t words,
-                int64_t row_bstep, cudaStream_t stream) {
+                int64_t row_bstep, cudaStream_t stream, void* ws, size_t ws_bytes) {
     if (n_rows < 0 || row_len < 1 || row_stride < row_len)
         return fail(DSA_ERR_INVALID, "topk_select: need n_rows >= 0, row_len >= 1, row_stride >= row_len");
     if (k < 1 || k > row_len)
@@ -1369,6 +1792,10 @@ int topk_select(const float* scores, int64_t n_rows, int64_t row_len, int64_t ro
     // other kernels take get it from kept_bitmap_kernel afterwards
     const bool cta_kernel = longest > 4096 && longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH");
     if (bits && cta_kernel) a.bits = bits;
+    // bitmap-only rows with a workspace: the sweep kernel and the per-row resolver
+    if (a.bits && !idx && longest > 4096 && ws && ws_bytes >= sweep_ws_bytes(n_rows, words) &&
+        !getenv("DSA_TOPK_ONE_KERNEL"))
+        return launch_sweep_resolve(a, ws, stream);
     int rc = topk_launch(a, longest, stream);
     if (rc || !bits || cta_kernel) return rc;
     // causal rows: key s kept only if s <= q_row0 + r % rows_per_batch;
@@ -1390,6 +1817,7 @@ static int topk_launch(TopkArgs& a, int64_t longest, cudaStream_t stream) {
     if (longest <= 4096 && !getenv("DSA_TOPK_LONG_PATH") && !getenv("DSA_TOPK_NO_WL2"))
         return launch_warp_l2(a, stream);
     if (longest <= kRowCache && !getenv("DSA_TOPK_LONG_PATH")) {
+        // bitmap-only rows (the forward's): the fine-digit two-sweep kernel
         if (longest <= 2048) return launch_cached<128, true>(a, longest, stream);
         // bitmap-only rows of 4K-8K: 128-thread CTAs re-reading the row from L2,
         // with a candidate buffer of longest/8 keys, instead of 256 threads

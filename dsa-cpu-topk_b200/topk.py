@@ -53,12 +53,15 @@ def topk_select(scores: torch.Tensor, k: int, *, causal: bool = False, q_row0: i
     return thr, idx, cnt
 
 
-def topk_select_bitmap(scores: torch.Tensor, k: int, *, causal: bool = True, q_row0: int = 0):
+def topk_select_bitmap(scores: torch.Tensor, k: int, *, causal: bool = True, q_row0: int = 0,
+                       workspace: bool = True):
     """scores [B, T_q, N] fp32 CUDA -> (thr [rows], cnt [rows] int32, bits [rows, words] int32).
 
     The kept set of each row (score >= thr, and s <= q_row0 + t when causal)
-    as the bitmap of dsa_attention.kept_bitmap, written by the top-K kernel
-    itself where the row length allows (4K-32K entries)."""
+    as the bitmap of dsa_attention.kept_bitmap, written by the top-K kernels
+    themselves where the row length allows (4K-32K entries).  workspace=True
+    gives them a candidate workspace (the sweep + resolve kernels); False runs
+    the one-kernel form that needs none."""
     assert scores.is_cuda and scores.dtype == torch.float32 and scores.dim() == 3, \
         "scores must be fp32 CUDA [B, T_q, N]"
     B, T_q, N = scores.shape
@@ -67,7 +70,11 @@ def topk_select_bitmap(scores: torch.Tensor, k: int, *, causal: bool = True, q_r
     thr = torch.empty(B * T_q, device=s.device, dtype=torch.float32)
     cnt = torch.empty(B * T_q, device=s.device, dtype=torch.int32)
     bits = torch.empty((B * T_q, _native.bitmap_words(N)), device=s.device, dtype=torch.int32)
-    _native.topk_select_bitmap(s, k, thr, bits, cnt, causal=causal, q_row0=q_row0)
+    ws = None
+    if workspace:
+        ws = torch.empty(_native.topk_select_bitmap_workspace_bytes(B * T_q, bits.shape[-1]),
+                         device=s.device, dtype=torch.uint8)
+    _native.topk_select_bitmap(s, k, thr, bits, cnt, causal=causal, q_row0=q_row0, workspace=ws)
     return thr, cnt, bits
 
 
