@@ -217,6 +217,9 @@ class Pipeline:
         if self.tc:
             for p in self.parts:
                 p["bits"] = torch.empty((p["NB"] * p["Tq"], self.words), device=dev, dtype=torch.int32)
+                # the top-K's candidate lists (sweep + resolve kernels)
+                p["tws"] = torch.empty(_native.topk_select_bitmap_workspace_bytes(p["NB"] * p["Tq"], self.words),
+                                       device=dev, dtype=torch.uint8)
                 # stage 3's workspace: block summary, fp16 copy of V (bf16)
                 nws = _native.sparse_attn_bitmap_workspace_bytes(p["NB"], p["Tq"], T, Q.shape[2], V.shape[3],
                                                                  _native.dtype_code(Q))
@@ -226,8 +229,11 @@ class Pipeline:
         # stage 3 with its workspace: block summary (+ |V| max and fp16 conversion
         # for bf16) + attention
         v16 = self.tc and Q.dtype == torch.bfloat16
+        # the bitmap top-K of rows longer than 4K (up to 32K) is two kernels (sweep + resolve)
+        two = sum(1 for p in self.parts
+                  if 4096 < min(T, p["q0"] + (p["NB"] - 1) * p["bstep"] + p["Tq"]) <= 32768) if self.tc else 0
         self.launches_per_step = (len(self.stage_names) + (1 if self.v16 else 0) + (2 if v16 else 0)) * \
-            len(self.parts)
+            len(self.parts) + two
         # opt-in one-launch kernel for short sequences (DSA_FUSED_SMALL=1)
         self.fused = T <= 512 and bool(os.environ.get("DSA_FUSED_SMALL")) and not self.stacked
         if self.fused:
@@ -267,8 +273,8 @@ class Pipeline:
             rec(1)
             NB, Tq, T = p["scores"].shape
             if self.tc:
-                n.topk_select_ex(p["scores"], NB * Tq, T, T, self.k, p["thr"], None, None, 0, p["bits"],
-                                 causal=True, rows_per_batch=Tq, q_row0=q0, row_bstep=bs)
+                n.topk_select_bitmap(p["scores"], self.k, p["thr"], p["bits"], causal=True, q_row0=q0,
+                                     row_bstep=bs, workspace=p["tws"])
                 rec(2)
                 n.sparse_attn_bitmap_ex(p["bits"], p["Q"], self.K, self.V, p["O"], q_row0=q0, row_bstep=bs,
                                         workspace=p["ws"])
@@ -557,7 +563,7 @@ def run_b200(args, cfg, world, rank, local):
                             traffic=traffic.get("sparse_attn")),
     }
     if pipe.tc:
-        stages["topk"]["kernel"] = "topk_cached_kernel (threshold + kept-set bitmap)"
+        stages["topk"]["kernel"] = "topk_sweep_kernel + topk_resolve_kernel (threshold + kept-set bitmap)"
         stages["sparse_attn"] = dict(
             bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_peak,
             unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc2_kernel", traffic=traffic.get("sparse_attn"),

@@ -73,7 +73,7 @@ def lib() -> ctypes.CDLL:
                                              f32, i32, p]
         L.dsa_topk_select_bitmap_workspace_bytes.argtypes = [i64, i64]
         L.dsa_topk_select_bitmap_workspace_bytes.restype = sz
-        L.dsa_topk_select_bitmap_ws.argtypes = [p, i64, i64, i64, i64, i32, i64, p, p, p, i64, p, sz, p]
+        L.dsa_topk_select_bitmap_ws.argtypes = [p, i64, i64, i64, i64, i64, i32, i64, p, p, p, i64, p, sz, p]
         L.dsa_device_status.argtypes = [p]
         L.dsa_device_status.restype = i32
         L.dsa_forward_workspace_bytes.argtypes = [i64, i64, i64, i64]
@@ -215,18 +215,21 @@ def topk_select_bitmap_workspace_bytes(n_rows, words):
     return int(lib().dsa_topk_select_bitmap_workspace_bytes(n_rows, words))
 
 
-def topk_select_bitmap(scores, k, thr, bits, cnt=None, *, causal=True, q_row0=0, workspace=None):
+def topk_select_bitmap(scores, k, thr, bits, cnt=None, *, causal=True, q_row0=0, row_bstep=0,
+                       workspace=None):
     """Threshold (+ count) and kept-set bitmap of every row of scores [B, T_q, T_k].
 
     With a workspace (uint8 CUDA tensor of topk_select_bitmap_workspace_bytes)
     rows of 4K-32K entries take the sweep + resolve kernels."""
     B, T_q, T_k = scores.shape
     if workspace is None:
+        assert row_bstep == 0, "row_bstep needs the workspace form"
         _check(lib().dsa_topk_select_bitmap(_ptr(scores), B * T_q, T_k, T_q, q_row0, int(bool(causal)), k,
                                             _ptr(thr), _ptr(cnt), _ptr(bits), bits.shape[-1], _stream()),
                "dsa_topk_select_bitmap")
         return
-    _check(lib().dsa_topk_select_bitmap_ws(_ptr(scores), B * T_q, T_k, T_q, q_row0, int(bool(causal)), k,
+    _check(lib().dsa_topk_select_bitmap_ws(_ptr(scores), B * T_q, T_k, T_q, q_row0, row_bstep,
+                                           int(bool(causal)), k,
                                            _ptr(thr), _ptr(cnt), _ptr(bits), bits.shape[-1], _ptr(workspace),
                                            workspace.numel(), _stream()),
            "dsa_topk_select_bitmap_ws")

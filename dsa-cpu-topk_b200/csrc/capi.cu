@@ -263,18 +263,20 @@ size_t dsa_topk_select_bitmap_workspace_bytes(int64_t n_rows, int64_t words_per_
 }
 
 int dsa_topk_select_bitmap_ws(const float* scores, int64_t n_rows, int64_t row_len,
-                              int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
-                              float* thr_out, int32_t* cnt_out, uint32_t* bits, int64_t words_per_row,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+                              int64_t rows_per_batch, int64_t q_row0, int64_t row_bstep, int causal,
+                              int64_t k, float* thr_out, int32_t* cnt_out, uint32_t* bits,
+                              int64_t words_per_row, void* workspace, size_t workspace_bytes,
+                              void* stream) {
     clear_error();
     if (!bits) return fail(DSA_ERR_INVALID, "topk_select_bitmap: bits is required");
+    if (row_bstep < 0) return fail(DSA_ERR_INVALID, "topk_select_bitmap: row_bstep must be >= 0");
     if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return fail(DSA_ERR_INVALID, "topk_select_bitmap: workspace must be 256-byte aligned");
     if (n_rows > 0 && workspace_bytes < dsa_topk_select_bitmap_workspace_bytes(n_rows, words_per_row))
         return fail(DSA_ERR_INVALID, "topk_select_bitmap: workspace too small");
     return topk_select(scores, n_rows, row_len, row_len, rows_per_batch, q_row0, causal, k, thr_out,
-                       nullptr, cnt_out, 0, bits, words_per_row, 0, (cudaStream_t)stream, workspace,
-                       workspace_bytes);
+                       nullptr, cnt_out, 0, bits, words_per_row, row_bstep, (cudaStream_t)stream,
+                       workspace, workspace_bytes);
 }
 
 int dsa_sparse_attn_ex(const int32_t* idx, const int32_t* cnt, int64_t idx_cap, const float* scores,

@@ -1321,15 +1321,18 @@ constexpr int kSweepDBits = 12;
 int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
     const CandLists cl = cand_lists(ws, a.n_rows, a.words);
     {
-        constexpr int BLOCK = 256;
-        // 6 CTAs of 256 threads per SM (40 registers; more CTAs spill, fewer measured slower)
-        auto kern = topk_sweep_kernel<BLOCK, kSweepDBits, 4, 6, 4>;
+        // 6 CTAs of 256 threads per SM (40 registers).  Measured on B200 at c5:
+        // 512- or 1024-thread CTAs, 128-thread CTAs, more loads in flight in
+        // sweep 2, chunks in reverse order and words kept in registers
+        // instead of shared memory were all slower or equal.
+        auto kern = topk_sweep_kernel<256, kSweepDBits, 4, 6, 4>;
+        const int block = 256;
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, BLOCK, 0) != cudaSuccess || per_sm < 1)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, block, 0) != cudaSuccess || per_sm < 1)
             per_sm = 1;
         int64_t grid = (int64_t)num_sms() * per_sm;
         if (grid > a.n_rows) grid = a.n_rows;
-        kern<<<(unsigned)grid, BLOCK, 0, stream>>>(a, cl);
+        kern<<<(unsigned)grid, block, 0, stream>>>(a, cl);
         if (int rc = check_launch("topk_sweep_kernel")) return rc;
     }
     {

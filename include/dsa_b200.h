@@ -277,7 +277,8 @@ DSA_API int dsa_topk_select_bitmap(const float* scores, int64_t n_rows, int64_t 
                                    float* thr_out, int32_t* cnt_out, uint32_t* bits,
                                    int64_t words_per_row, void* stream);
 
-/* dsa_topk_select_bitmap with a workspace of
+/* dsa_topk_select_bitmap with row blocks (row_bstep as in dsa_topk_select_ex)
+ * and a workspace of
  * dsa_topk_select_bitmap_workspace_bytes(n_rows, words_per_row) bytes (256-byte
  * aligned).  Rows of 4K-32K entries then take two kernels: a sweep kernel that
  * writes the final bits of every score above the threshold's first-digit bin
@@ -287,10 +288,10 @@ DSA_API int dsa_topk_select_bitmap(const float* scores, int64_t n_rows, int64_t 
  * interface (dsa_attention.py:343-344 threshold + :230-324 mask). */
 DSA_API size_t dsa_topk_select_bitmap_workspace_bytes(int64_t n_rows, int64_t words_per_row);
 DSA_API int dsa_topk_select_bitmap_ws(const float* scores, int64_t n_rows, int64_t row_len,
-                                      int64_t rows_per_batch, int64_t q_row0, int causal, int64_t k,
-                                      float* thr_out, int32_t* cnt_out, uint32_t* bits,
-                                      int64_t words_per_row, void* workspace, size_t workspace_bytes,
-                                      void* stream);
+                                      int64_t rows_per_batch, int64_t q_row0, int64_t row_bstep,
+                                      int causal, int64_t k, float* thr_out, int32_t* cnt_out,
+                                      uint32_t* bits, int64_t words_per_row, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 DSA_API int dsa_sparse_attn_bitmap(const uint32_t* bits, int64_t words_per_row,
                                    const void* Q, const void* K, const void* V, float* O,
