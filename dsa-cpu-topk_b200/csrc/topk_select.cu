@@ -1323,8 +1323,9 @@ int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
     {
         // 6 CTAs of 256 threads per SM (40 registers).  Measured on B200 at c5:
         // 512- or 1024-thread CTAs, 128-thread CTAs, more loads in flight in
-        // sweep 2, chunks in reverse order and words kept in registers
-        // instead of shared memory were all slower or equal.
+        // sweep 2, chunks in reverse order, words kept in registers instead
+        // of shared memory, and rows taken in a short/long interleaved order
+        // (less L2 missing in sweep 2, but slower) were all slower or equal.
         auto kern = topk_sweep_kernel<256, kSweepDBits, 4, 6, 4>;
         const int block = 256;
         int per_sm = 0;
