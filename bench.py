@@ -235,7 +235,7 @@ class Pipeline:
         self.launches_per_step = (len(self.stage_names) + (1 if self.v16 else 0) + (2 if v16 else 0)) * \
             len(self.parts) + two
         # opt-in one-launch kernel for short sequences (DSA_FUSED_SMALL=1)
-        self.fused = T <= 512 and bool(os.environ.get("DSA_FUSED_SMALL")) and not self.stacked
+        self.fused = T <= 2048 and bool(os.environ.get("DSA_FUSED_SMALL")) and not self.stacked
         if self.fused:
             from dsa_attention import forward_workspace_bytes
             self.ws = [torch.empty(forward_workspace_bytes(B, p["Tq"], T, self.k), device=dev, dtype=torch.uint8)
@@ -549,38 +549,41 @@ def run_b200(args, cfg, world, rank, local):
                 "sustained bf16 GEMM peak (SM clock below 95% of max)")
     alg = pipe.algorithmic(cfg)
     traffic = load_traffic().get(args.config, {})
-    stages = {
-        "indexer": dict(bound="tensor", achieved=alg["indexer_flops"] / (stage_ms[0] / 1e3) / 1e12,
-                        peak=tf_peak * (2 if cfg.get("idx_dtype") == "fp8" else 1), unit="TFLOP/s",
-                        ms=stage_ms[0],
-                        kernel=("indexer_tc (e4m3, kind::f8f6f4)" if cfg.get("idx_dtype") == "fp8" else
-                                "indexer_tc" if cfg["dtype"] == "bf16" else "indexer_simt (fp32 CUDA cores)"),
-                        traffic=traffic.get("indexer")),
-        "topk": dict(bound="hbm", achieved=alg["topk_bytes"] / (stage_ms[1] / 1e3) / 1e9, peak=hbm,
-                     unit="GB/s", ms=stage_ms[1], kernel="topk_select_kernel", traffic=traffic.get("topk")),
-        "sparse_attn": dict(bound="hbm", achieved=alg["attn_bytes"] / (stage_ms[-1] / 1e3) / 1e9, peak=hbm,
-                            unit="GB/s", ms=stage_ms[-1], kernel="sparse_attn_kernel",
-                            traffic=traffic.get("sparse_attn")),
-    }
-    if pipe.tc:
-        stages["topk"]["kernel"] = "topk_sweep_kernel + topk_resolve_kernel (threshold + kept-set bitmap)"
-        stages["sparse_attn"] = dict(
-            bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_peak,
-            unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc2_kernel", traffic=traffic.get("sparse_attn"),
-            note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs",
-            useful_tflops=alg["attn_flops"] / (stage_ms[2] / 1e3) / 1e12,
-            useful_fraction_of_tile_flops=alg["attn_flops"] / max(alg["attn_tile_flops"], 1.0))
-        stages["sparse_attn"]["useful_frac"] = stages["sparse_attn"]["useful_tflops"] / tf_peak
-    for v in stages.values():
-        v["frac"] = v["achieved"] / v["peak"]
-        if v["unit"] == "TFLOP/s":
-            mult = 2 if v is stages.get("indexer") and cfg.get("idx_dtype") == "fp8" else 1
-            v["frac_of_burst"] = v["achieved"] / (tflops * mult)
-            v["frac_of_sustained"] = v["achieved"] / (tf_sust * mult)
-            v["peak_source"] = tf_label + (" (MEASURED_PEAKS.json)" if src == "measured" else "")
-        else:
-            v["peak_source"] = "measured copy bandwidth (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
-    if cfg.get("idx_dtype") == "fp8":
+    if pipe.fused:
+        stages = {}   # filled below
+    else:
+        stages = {
+            "indexer": dict(bound="tensor", achieved=alg["indexer_flops"] / (stage_ms[0] / 1e3) / 1e12,
+                            peak=tf_peak * (2 if cfg.get("idx_dtype") == "fp8" else 1), unit="TFLOP/s",
+                            ms=stage_ms[0],
+                            kernel=("indexer_tc (e4m3, kind::f8f6f4)" if cfg.get("idx_dtype") == "fp8" else
+                                    "indexer_tc" if cfg["dtype"] == "bf16" else "indexer_simt (fp32 CUDA cores)"),
+                            traffic=traffic.get("indexer")),
+            "topk": dict(bound="hbm", achieved=alg["topk_bytes"] / (stage_ms[1] / 1e3) / 1e9, peak=hbm,
+                         unit="GB/s", ms=stage_ms[1], kernel="topk_select_kernel", traffic=traffic.get("topk")),
+            "sparse_attn": dict(bound="hbm", achieved=alg["attn_bytes"] / (stage_ms[-1] / 1e3) / 1e9, peak=hbm,
+                                unit="GB/s", ms=stage_ms[-1], kernel="sparse_attn_kernel",
+                                traffic=traffic.get("sparse_attn")),
+        }
+        if pipe.tc:
+            stages["topk"]["kernel"] = "topk_sweep_kernel + topk_resolve_kernel (threshold + kept-set bitmap)"
+            stages["sparse_attn"] = dict(
+                bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_peak,
+                unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc2_kernel", traffic=traffic.get("sparse_attn"),
+                note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs",
+                useful_tflops=alg["attn_flops"] / (stage_ms[2] / 1e3) / 1e12,
+                useful_fraction_of_tile_flops=alg["attn_flops"] / max(alg["attn_tile_flops"], 1.0))
+            stages["sparse_attn"]["useful_frac"] = stages["sparse_attn"]["useful_tflops"] / tf_peak
+        for v in stages.values():
+            v["frac"] = v["achieved"] / v["peak"]
+            if v["unit"] == "TFLOP/s":
+                mult = 2 if v is stages.get("indexer") and cfg.get("idx_dtype") == "fp8" else 1
+                v["frac_of_burst"] = v["achieved"] / (tflops * mult)
+                v["frac_of_sustained"] = v["achieved"] / (tf_sust * mult)
+                v["peak_source"] = tf_label + (" (MEASURED_PEAKS.json)" if src == "measured" else "")
+            else:
+                v["peak_source"] = "measured copy bandwidth (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
+    if cfg.get("idx_dtype") == "fp8" and not pipe.fused:
         stages["indexer"]["peak_source"] += "; FP8 peak taken as 2x the bf16 one (none measured)"
     if pipe.fused:
         elt = 2 if cfg["dtype"] == "bf16" else 4

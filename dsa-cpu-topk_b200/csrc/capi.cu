@@ -3,6 +3,7 @@
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <string>
 
@@ -433,13 +434,18 @@ int dsa_forward_ex(const void* q_idx, const void* k_idx, const float* w_idx, con
     int32_t* idx = reinterpret_cast<int32_t*>(ws + W.idx);
     const int64_t k = top_k < T_k ? top_k : T_k;
 
-    // Opt-in (DSA_FUSED_SMALL=1): short sequences in one fused launch, contiguous
-    // inputs only.  Measured slower than the three stage kernels on B200 (c1:
-    // 0.14 vs 0.117 ms), so the default stays the three-stage pipeline.
-    if (getenv("DSA_FUSED_SMALL") && !layout) {
+    // Opt-in (DSA_FUSED_SMALL=1): short sequences (T_k <= 2048) in one fused
+    // launch, contiguous inputs only.  Measured slower than the three stage
+    // kernels on B200 (c1: 0.14 vs 0.117 ms), so the default stays the
+    // three-stage pipeline.  DSA_FUSED_SMALL=require makes a shape outside the
+    // fused kernel's limits an error instead of a fall-back (tests).
+    const char* fs = getenv("DSA_FUSED_SMALL");
+    if (fs && !layout) {
         rc = fused_small_forward(q_idx, k_idx, w_idx, Q, K, V, O, B, T_q, T_k, q_row0, HI, DI, HQ, DQ,
                                  DV, k, idx_dtype, qkv_dtype, st);
         if (rc != -100) return rc;
+        if (!strcmp(fs, "require"))
+            return fail(DSA_ERR_UNSUPPORTED, "dsa_forward: shape outside the fused small-T kernel's limits");
     }
 
     rc = run_indexer(q_idx, k_idx, w_idx, scores, B, T_q, T_k, q_row0, HI, DI, idx_dtype,
