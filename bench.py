@@ -303,7 +303,17 @@ class Pipeline:
                 flops += 2.0 * HI * DI * valid
                 topk_b += 4.0 * valid
                 # tensor-core stage 3: every 128x128 (query, key) tile up to the
-                # diagonal is two MMAs of 2*128*128*D FLOPs per head
+                # diagonal is two MMAs of 2*128*128*D FLOPs per head; with its
+                # workspace the kernel skips the key blocks that hold no kept key
+                # of the query tile, so those are counted from the bitmap
+                if self.tc and p.get("ws") is not None:
+                    nbk = self.words // 4
+                    kb = p["bits"][bb * Tq:(bb + 1) * Tq].view(Tq, nbk, 4).ne(0).any(-1)
+                    pad = (-Tq) % 128
+                    if pad:
+                        kb = torch.cat([kb, kb.new_zeros((pad, nbk))])
+                    tile_f += HQ * 4.0 * 128 * 128 * D * kb.view(-1, 128, nbk).any(1).sum().item()
+                    continue
                 for qt in range((Tq + 127) // 128):
                     t_end = r0 + min((qt + 1) * 128, Tq)
                     nblk = min((t_end - 1) // 128 + 1, (T + 127) // 128)
@@ -570,7 +580,7 @@ def run_b200(args, cfg, world, rank, local):
             stages["sparse_attn"] = dict(
                 bound="tensor", achieved=alg["attn_tile_flops"] / (stage_ms[2] / 1e3) / 1e12, peak=tf_peak,
                 unit="TFLOP/s", ms=stage_ms[2], kernel="attn_tc2_kernel", traffic=traffic.get("sparse_attn"),
-                note="FLOPs of the causal 128x128 tiles (QK^T and PV) the masked flash attention runs",
+                note="FLOPs of the 128x128 (query, key) tiles (QK^T and PV) the masked flash attention runs: the causal tiles holding a kept key",
                 useful_tflops=alg["attn_flops"] / (stage_ms[2] / 1e3) / 1e12,
                 useful_fraction_of_tile_flops=alg["attn_flops"] / max(alg["attn_tile_flops"], 1.0))
             stages["sparse_attn"]["useful_frac"] = stages["sparse_attn"]["useful_tflops"] / tf_peak
