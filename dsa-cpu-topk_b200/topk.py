@@ -94,3 +94,35 @@ def topk_threshold_batch_merge(scores: torch.Tensor, k: int) -> torch.Tensor:
 def select_threshold(scores: torch.Tensor, top_k: int) -> torch.Tensor:
     """dsa_attention.py:41-44: k_eff = min(top_k, N); returns thr [..., 1]."""
     return topk_threshold(scores, min(top_k, scores.shape[-1]))
+
+
+if __name__ == "__main__":
+    # Timing driver for the forward's bitmap top-K: causal rows of N(0,1)
+    # scores [B, T, T], k per row, the sweep + resolve kernels (workspace)
+    # checked bit for bit against the one-kernel form, then timed with CUDA
+    # events, L2 flushed between runs.
+    import argparse
+
+    ap = argparse.ArgumentParser(description="time topk_select_bitmap on causal N(0,1) rows")
+    ap.add_argument("--B", type=int, default=1)
+    ap.add_argument("--T", type=int, default=32768)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--runs", type=int, default=10)
+    args = ap.parse_args()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    s = torch.randn((args.B, args.T, args.T), device="cuda", generator=g)
+    one = topk_select_bitmap(s, args.k, workspace=False)
+    two = topk_select_bitmap(s, args.k)
+    assert all(torch.equal(x, y) for x, y in zip(one, two)), "sweep + resolve differs from the one-kernel form"
+    flush = torch.empty(256 << 20, device="cuda", dtype=torch.uint8)
+    ts = []
+    for i in range(args.runs + 2):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        topk_select_bitmap(s, args.k)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ts = sorted(ts[2:])
+    print(f"topk_select_bitmap B={args.B} T={args.T} k={args.k}: min {ts[0]:.3f} ms, median {ts[len(ts) // 2]:.3f} ms")
