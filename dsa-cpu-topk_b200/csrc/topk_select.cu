@@ -1015,10 +1015,14 @@ struct CandLists {
     int cap;
 };
 
-// candidates a row may hold: 1/16 of its positions, 256..1024
+// candidates a row may hold: 1/8 of its positions, 256..2048.  On the
+// indexer's scores of a c5 sequence (t up to 32K, k = 2048) the threshold's
+// 12-bit bin holds up to ~1,250 keys (about 3% of the row: those scores are
+// wide relative to the threshold); with 1/16 (at most 1,024) about 5% of the
+// long rows overflowed into the exact per-row path
 __host__ __device__ inline int cand_cap_for(int64_t words) {
-    const int64_t c = words * 2;
-    return (int)(c < 256 ? 256 : c > 1024 ? 1024 : c);
+    const int64_t c = words * 4;
+    return (int)(c < 256 ? 256 : c > 2048 ? 2048 : c);
 }
 
 inline size_t align256_sz(size_t x) { return (x + 255) / 256 * 256; }

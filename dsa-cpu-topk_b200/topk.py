@@ -108,21 +108,48 @@ if __name__ == "__main__":
     ap.add_argument("--T", type=int, default=32768)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--runs", type=int, default=10)
+    ap.add_argument("--zigzag", default=None, metavar="N:r",
+                    help="only the rows rank r of N owns under the zig-zag split of one sequence "
+                         "(two row blocks, one call with row_bstep)")
     args = ap.parse_args()
     g = torch.Generator(device="cuda").manual_seed(0)
-    s = torch.randn((args.B, args.T, args.T), device="cuda", generator=g)
-    one = topk_select_bitmap(s, args.k, workspace=False)
-    two = topk_select_bitmap(s, args.k)
-    assert all(torch.equal(x, y) for x, y in zip(one, two)), "sweep + resolve differs from the one-kernel form"
+    if args.zigzag:
+        from sharding import zigzag_plan
+        n, r = (int(x) for x in args.zigzag.split(":"))
+        b0, b1 = zigzag_plan(args.T, n)[r]
+        assert b0.stop - b0.start == b1.stop - b1.start, "zig-zag blocks of equal rows"
+        s = torch.randn((2, b0.stop - b0.start, args.T), device="cuda", generator=g)
+        q_row0, bstep = b0.start, b1.start - b0.start
+    else:
+        s = torch.randn((args.B, args.T, args.T), device="cuda", generator=g)
+        q_row0, bstep = 0, 0
+    B_, T_q, N = s.shape
+    words = _native.bitmap_words(N)
+
+    def run(ws):
+        thr = torch.empty(B_ * T_q, device="cuda", dtype=torch.float32)
+        cnt = torch.empty(B_ * T_q, device="cuda", dtype=torch.int32)
+        bits = torch.empty((B_ * T_q, words), device="cuda", dtype=torch.int32)
+        _native.topk_select_bitmap(s, args.k, thr, bits, cnt, causal=True, q_row0=q_row0, row_bstep=bstep,
+                                   workspace=ws)
+        return thr, cnt, bits
+
+    ws = torch.empty(_native.topk_select_bitmap_workspace_bytes(B_ * T_q, words), device="cuda",
+                     dtype=torch.uint8)
+    if bstep == 0:
+        one = run(None)
+        two = run(ws)
+        assert all(torch.equal(x, y) for x, y in zip(one, two)), "sweep + resolve differs from the one-kernel form"
     flush = torch.empty(256 << 20, device="cuda", dtype=torch.uint8)
     ts = []
     for i in range(args.runs + 2):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        topk_select_bitmap(s, args.k)
+        run(ws)
         e1.record()
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1))
     ts = sorted(ts[2:])
-    print(f"topk_select_bitmap B={args.B} T={args.T} k={args.k}: min {ts[0]:.3f} ms, median {ts[len(ts) // 2]:.3f} ms")
+    print(f"topk_select_bitmap B={B_} T_q={T_q} N={N} k={args.k} zigzag={args.zigzag}: "
+          f"min {ts[0]:.3f} ms, median {ts[len(ts) // 2]:.3f} ms")
