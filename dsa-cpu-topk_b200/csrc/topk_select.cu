@@ -1320,9 +1320,9 @@ __global__ void __launch_bounds__(256, 4) topk_resolve_kernel(TopkArgs a, CandLi
     }
 }
 
-constexpr int kSweepDBits = 12;
 
-int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
+template <int DB>
+int launch_sweep_resolve_t(const TopkArgs& a, void* ws, cudaStream_t stream) {
     const CandLists cl = cand_lists(ws, a.n_rows, a.words);
     {
         // 6 CTAs of 256 threads per SM (40 registers).  Measured on B200 at c5:
@@ -1330,7 +1330,7 @@ int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
         // sweep 2, chunks in reverse order, words kept in registers instead
         // of shared memory, and rows taken in a short/long interleaved order
         // (less L2 missing in sweep 2, but slower) were all slower or equal.
-        auto kern = topk_sweep_kernel<256, kSweepDBits, 4, 6, 4>;
+        auto kern = topk_sweep_kernel<256, DB, 4, 6, 4>;
         const int block = 256;
         int per_sm = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, block, 0) != cudaSuccess || per_sm < 1)
@@ -1341,7 +1341,7 @@ int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
         if (int rc = check_launch("topk_sweep_kernel")) return rc;
     }
     {
-        auto kern = topk_resolve_kernel<kSweepDBits>;
+        auto kern = topk_resolve_kernel<DB>;
         const size_t smem = 8 * ((size_t)cl.cap + 256) * sizeof(uint32_t);
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return fail(DSA_ERR_CUDA, "topk_resolve: cannot set dynamic shared memory size");
@@ -1354,6 +1354,18 @@ int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
         kern<<<(unsigned)grid, 256, smem, stream>>>(a, cl);
         return check_launch("topk_resolve_kernel");
     }
+}
+
+// First-digit width by row length.  Rows of up to 8K entries (c4) take 11 bits:
+// a 2048-bin histogram halves the per-row scan between the sweeps, which
+// shorter rows pay on fewer bytes (c4 top-K 0.413 -> 0.357 ms); longer rows
+// (c5) take 12, since 11 doubles their threshold bin's candidates and long
+// rows of the indexer's scores then overflow the list (c5 1.05 -> 1.28 ms).
+// 10 bits measured slower at c4 (0.425 ms).  DSA_TOPK_SWEEP_DBITS=11|12 forces one.
+int launch_sweep_resolve(const TopkArgs& a, void* ws, cudaStream_t stream) {
+    static const int forced = [] { const char* e = getenv("DSA_TOPK_SWEEP_DBITS"); return e ? atoi(e) : 0; }();
+    const int db = forced ? forced : (a.words * 32 <= 8192 ? 11 : 12);
+    return db == 11 ? launch_sweep_resolve_t<11>(a, ws, stream) : launch_sweep_resolve_t<12>(a, ws, stream);
 }
 
 // ===========================================================================
