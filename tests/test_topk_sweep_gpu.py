@@ -19,6 +19,8 @@ def make(kind, B, Tq, T, seed, cuda):
         x = (x * 4).round() / 4
     elif kind == "heavy":         # wide dynamic range: crowded first-digit bins
         x = torch.exp(x * 6)
+    elif kind == "wide":          # like the indexer's c5 scores: the threshold's bin holds ~3% of a row
+        x = 6.0 + 8.0 * x
     elif kind == "special":
         x[:, ::97, ::13] = float("nan")
         x[:, 5::89, 3::17] = float("inf")
@@ -34,7 +36,7 @@ def both(x, k, q_row0):
     return a, b
 
 
-@pytest.mark.parametrize("kind", ["randn", "relu", "ties", "heavy", "special"])
+@pytest.mark.parametrize("kind", ["randn", "relu", "ties", "heavy", "wide", "special"])
 @pytest.mark.parametrize("B,Tq,T,k,q_row0", [(1, 8192, 8192, 512, 0), (2, 3000, 6000, 300, 3000),
                                               (1, 2048, 32768, 2048, 30720), (1, 1024, 16384, 4096, 9000)])
 def test_sweep_resolve_equals_one_kernel(cuda, kind, B, Tq, T, k, q_row0):
