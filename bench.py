@@ -104,7 +104,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         time.sleep(0.3)
@@ -115,7 +115,10 @@ class ClockSampler:
         time.sleep(0.25)
         self.proc.terminate()
         self.proc.wait()
-        sm, mx, reasons = [], [], set()
+        # Samples every 50 ms; the median is taken over the samples drawn under
+        # load (board power at least half of the run's highest sample), so the
+        # idle moments before and after the timed region do not count.
+        rows = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
             for line in f:
@@ -123,17 +126,25 @@ class ClockSampler:
                 if len(c) < 9:
                     continue
                 try:
-                    sm.append(float(c[1].split()[0]))
-                    mx.append(float(c[2].split()[0]))
+                    sm_v, mx_v = float(c[1].split()[0]), float(c[2].split()[0])
                 except ValueError:
                     continue
-                for n, v in zip(names, c[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
+                try:
+                    pw = float(c[3].split()[0])
+                except ValueError:
+                    pw = None
+                rows.append((sm_v, mx_v, pw, [n for n, v in zip(names, c[5:9]) if v.lower().startswith("active")]))
         os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0, "reasons": []}
+        pmax = max((r[2] for r in rows if r[2] is not None), default=None)
+        load = [r for r in rows if pmax is None or (r[2] is not None and r[2] >= 0.5 * pmax)] or rows
+        reasons = sorted({n for r in load for n in r[3]})
+        return {"sm_mhz": statistics.median(r[0] for r in load),
+                "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(load), "samples_all": len(rows),
+                "power_w_median": statistics.median(r[2] for r in load) if pmax is not None else None,
+                "reasons": reasons}
 
 
 # --------------------------------------------------------------------------
